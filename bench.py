@@ -1,0 +1,296 @@
+"""Benchmark of the auction LAP solver (one JSON line on rank 0).
+
+Workload: B=1, N=M=4096 fp32 uniform[0,1) costs (seed 1),
+epsilon scaling 1.0 -> 1e-2 by 0.25 ([1, .25, .0625, .015625, .01]), max_iter
+1000 per epsilon.  One step = one full solve.  With --gpus N (one process per
+GPU under torchrun) every rank solves its own replica (a single problem does
+not split across GPUs), and the batched config 4 (B=256, N=M=512, low-rank +
+noise) is additionally sharded over the ranks (256/N problems each) and
+reported under "batched".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's algorithm on the host CPU cores (the C
+restatement in oracle/, all host threads) on the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+METRIC = "auction LAP ms/solve at B=1 N=4096 fp32; batched solves/sec at 1/2/4/8 GPUs"
+N_MAIN = 4096
+DTYPE_BYTES = 4
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-batched", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons of one GPU while running."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5).stdout
+                f = [x.strip() for x in out.strip().split(",")]
+                if len(f) == 6:
+                    self.samples.append(f)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(s[0]) for s in self.samples if s[0].replace(".", "").isdigit()]
+        mx = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for s in self.samples for k in range(4) if s[2 + k].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def measured_peak_hbm():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "roofline_inputs.json")) as f:
+            return json.load(f).get("grid_kernel_cfg2_dram_bytes_per_launch")
+    except Exception:
+        return None
+
+
+def cpu_port_time(cost, sched, reps, threads):
+    from oracle import oracle
+    oracle.build()
+    times = []
+    stats = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        _, _, stats = oracle.solve(cost, sched, 1000, nthreads=threads)
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times) * 1e3, stats
+
+
+def run_reference(args):
+    """--impl reference: the reference algorithm (C restatement) on host cores."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    import efficient_linear_assignment_b200 as ela
+    cost = ela.workloads.cfg2()
+    sched = ela.workloads.CFG2_SCHEDULE
+    threads = os.cpu_count() or 1
+    cpu_port_time(cost, sched, max(1, args.warmup), threads)  # warm-up
+    ms, _ = cpu_port_time(cost, sched, args.steps, threads)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(ms, 4), "unit": "ms/solve",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded uniform[0,1), seed 1)",
+        "config": {"workload": "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps"},
+        "cpu_baseline": {"value": round(ms, 4), "unit": "ms/solve", "cores": threads, "kind": "port",
+                         "sample": "one full cfg2 solve per step (median of steps)"},
+        "e2e": {"value": round(ms, 4), "unit": "ms/solve", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+
+    import efficient_linear_assignment_b200 as ela
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sched = ela.workloads.CFG2_SCHEDULE
+    cost_cpu = ela.workloads.cfg2()
+    cost = cost_cpu.to(dev)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return ela.auction_solve_op(cost, sched, 1000, ela.PATH_AUTO)
+
+    for _ in range(args.warmup):
+        a, p, st, status = step()
+    torch.cuda.synchronize()
+    ela._lib.check(int(status.item()), "warm-up solve")
+    row_bids = int(st[0, 1].item())
+    rounds = int(st[0, 0].item())
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for k in range(args.steps):
+            flush.zero_()
+            starts[k].record(stream)
+            a, p, st, status = step()
+            ends[k].record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    ela._lib.check(int(status.item()), "timed solve")
+    per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    ms_step = max_over_ranks(sum(per_step) / len(per_step))
+    value = ms_step / world  # ms per solve over the whole job (one solve per rank per step)
+
+    # roofline of the solve kernel: algorithmic cost bytes (row-bids x M x 4 B) per launch
+    peak, peak_kind = measured_peak_hbm()
+    alg_bytes = row_bids * N_MAIN * DTYPE_BYTES
+    achieved = alg_bytes / (statistics.mean(per_step) * 1e-3) / 1e9
+
+    # e2e through the public API: pinned host cost -> device, solve, indices -> pinned host
+    host_cost = cost_cpu.pin_memory()
+    host_idx = torch.empty((1, N_MAIN), dtype=torch.int64).pin_memory()
+    e2e_ms = []
+    for k in range(args.warmup + args.steps):
+        flush.zero_()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dcost = host_cost.to(dev, non_blocking=True)
+        idx = ela.linear_assignment(dcost, epsilon=sched, max_iter=1000)
+        host_idx.copy_(idx, non_blocking=True)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        if k >= args.warmup:
+            e2e_ms.append(e0.elapsed_time(e1))
+    e2e_val = max_over_ranks(statistics.mean(e2e_ms)) / world
+
+    # batched config 4, sharded over the ranks
+    batched = None
+    if not args.no_batched:
+        B4 = 256
+        per = B4 // world
+        c4 = ela.workloads.cfg4()[rank * per:(rank + 1) * per].contiguous().to(dev)
+        for _ in range(args.warmup):
+            r4 = ela.auction_solve_op(c4, [1e-2], 1000, ela.PATH_AUTO)
+        torch.cuda.synchronize()
+        b_ms = []
+        barrier()
+        for _ in range(args.steps):
+            flush.zero_()
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            r4 = ela.auction_solve_op(c4, [1e-2], 1000, ela.PATH_AUTO)
+            s1.record(stream)
+            torch.cuda.synchronize()
+            b_ms.append(s0.elapsed_time(s1))
+        barrier()
+        ela._lib.check(int(r4[3].item()), "batched solve")
+        bm = max_over_ranks(statistics.mean(b_ms))
+        batched = {"workload": "cfg4: B=256 N=M=512 fp32 low-rank+noise, eps 1e-2", "problems_per_gpu": per,
+                   "ms_per_step": round(bm, 4), "value": round(B4 / (bm * 1e-3), 2), "unit": "solves/sec",
+                   "scaling": "strong"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        cms, _ = cpu_port_time(cost_cpu, sched, 3, threads)
+        cpu = {"value": round(cms, 3), "unit": "ms/solve", "cores": threads, "kind": "port",
+               "sample": "full cfg2 solve, median of 3, C restatement of the reference (oracle/)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 5), "unit": "ms/solve", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded uniform[0,1), seed 1; cfg4 seed 3)",
+            "config": {"workload": "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps",
+                       "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) between steps",
+                       "rounds": rounds, "row_bids": row_bids},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(),
+                         "peak_kind": peak_kind,
+                         "alg_bytes_per_launch": alg_bytes},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 4), "unit": "ms/solve",
+                    "h2d_bytes_per_step": cost_cpu.numel() * 4, "d2h_bytes_per_step": N_MAIN * 8},
+            "gpu_launches": args.steps,
+            "batched": batched,
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,90 @@
+"""Public API: ``linear_assignment`` and its IMLE autograd, as in the reference.
+
+Mirrors src/efficient_linear_assignment/auction/api.py of the reference:
+same signature, shape check (N and M multiples of 8, ValueError otherwise),
+(B,N) int64 indices with unassigned rows reported as column 0 (the argmax of an
+all-zero one-hot row, api.py:64-71,174), or the differentiable (B,N,M) one-hot
+whose backward re-solves on ``C + lambda*G`` with lambda = 1 (api.py:82-149).
+"""
+from __future__ import annotations
+
+from typing import Sequence, Union
+
+import torch
+
+from .solver import AuctionB200
+
+# Backend registry (api.py:7-47).  Every name runs the B200 solver; 'torch'
+# is accepted because the results are those of the reference's torch backend.
+BACKENDS = {
+    "b200": AuctionB200,
+    "cuda": AuctionB200,
+    "cpp": AuctionB200,
+    "torch": AuctionB200,
+}
+
+
+def _one_hot(assignment: torch.Tensor, like: torch.Tensor) -> torch.Tensor:
+    """(B,N) columns -> (B,N,M) one-hot in like.dtype; rows at -1 stay zero."""
+    P = torch.zeros_like(like)
+    valid = assignment >= 0
+    P.scatter_(2, assignment.clamp(min=0).unsqueeze(2), valid.unsqueeze(2).to(like.dtype))
+    return P
+
+
+def _solver(backend_name: str, epsilon, max_iter: int):
+    if backend_name not in BACKENDS:
+        raise ValueError(f"Backend '{backend_name}' not available. Options: {list(BACKENDS.keys())}")
+    return BACKENDS[backend_name](epsilon=epsilon, max_iter=max_iter)
+
+
+class AuctionIMLE(torch.autograd.Function):
+    """Forward: hard assignment as a one-hot.  Backward: IMLE difference
+    ``P(C + lambda*G) - P(C)`` divided by lambda (reference api.py:49-149)."""
+
+    @staticmethod
+    def forward(ctx, cost_matrix, epsilon, max_iter, backend_name):
+        solver = _solver(backend_name, epsilon, max_iter)
+        assignment, _ = solver.solve(cost_matrix)
+        P = _one_hot(assignment, cost_matrix)
+        ctx.save_for_backward(cost_matrix, P)
+        ctx.epsilon = epsilon
+        ctx.max_iter = max_iter
+        ctx.backend_name = backend_name
+        ctx.imle_lambda = 1.0
+        return P
+
+    @staticmethod
+    def backward(ctx, grad_output):
+        cost_matrix, P_forward = ctx.saved_tensors
+        lam = ctx.imle_lambda
+        target_cost = cost_matrix + lam * grad_output
+        solver = _solver(ctx.backend_name, ctx.epsilon, ctx.max_iter)
+        assignment_t, _ = solver.solve(target_cost)
+        P_target = _one_hot(assignment_t, cost_matrix)
+        return (P_target - P_forward) / lam, None, None, None
+
+
+def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[float]] = 1e-2,
+                      max_iter: int = 1000, backend: str = "b200", return_indices: bool = True):
+    """Solve the linear assignment problem (minimise total cost) by auction.
+
+    cost_matrix: (B,N,M) or (N,M) CUDA tensor, fp32/fp16/bf16/fp64, N and M
+    multiples of 8.  epsilon: constant epsilon (the reference's only mode) or an
+    epsilon-scaling schedule.  Returns (B,N) int64 indices when return_indices,
+    else the differentiable (B,N,M) one-hot.
+    """
+    is_batched = cost_matrix.ndim == 3
+    if not is_batched:
+        cost_matrix = cost_matrix.unsqueeze(0)
+    _, N, M = cost_matrix.shape
+    if N % 8 != 0 or M % 8 != 0:
+        raise ValueError(f"Input dimensions must be multiples of 8. Got shape {cost_matrix.shape}. "
+                         "Please pad your input.")
+    if return_indices:
+        solver = _solver(backend, epsilon, max_iter)
+        assignment, _ = solver.solve(cost_matrix.detach())
+        idx = assignment.clamp(min=0)
+        return idx if is_batched else idx.squeeze(0)
+    P = AuctionIMLE.apply(cost_matrix, epsilon, max_iter, backend)
+    return P if is_batched else P.squeeze(0)

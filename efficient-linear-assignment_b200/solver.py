@@ -1,0 +1,129 @@
+"""Solver backend over the CUDA library.
+
+``AuctionB200`` is the drop-in for the reference's backend plug-in
+(``AuctionTorch`` / ``AuctionCPPCCUDA``: ``cls(epsilon, max_iter).solve(cost)
+-> (assignment (B,N) int64 with -1 = unassigned, prices (B,M))``,
+src/efficient_linear_assignment/auction/api.py:7-47,56-61 and
+src/efficient_linear_assignment/auction/cpp_backend.py:18-40).  The solve is
+the ``ela::auction_solve`` custom op, whose CUDA implementation calls
+``ela_auction_solve`` through the C ABI on the current stream.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence, Tuple, Union
+
+import torch
+
+from . import _lib
+
+DTYPE_CODE = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2, torch.float64: 3}
+
+EpsArg = Union[float, Sequence[float]]
+
+
+def _as_schedule(epsilon: EpsArg) -> list[float]:
+    if isinstance(epsilon, (int, float)):
+        return [float(epsilon)]
+    sched = [float(e) for e in epsilon]
+    if not sched:
+        raise ValueError("epsilon schedule is empty")
+    return sched
+
+
+@torch.library.custom_op("ela::auction_solve", mutates_args=())
+def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int) -> Tuple[
+        torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,))."""
+    if cost.device.type != "cuda":
+        raise RuntimeError("ela::auction_solve needs a CUDA tensor (there is no CPU path)")
+    if cost.dtype not in DTYPE_CODE:
+        raise TypeError(f"unsupported cost dtype {cost.dtype}")
+    if cost.dim() != 3:
+        raise ValueError("cost must be (B, N, M)")
+    if cost.stride(2) != 1:
+        cost = cost.contiguous()
+    lib = _lib.load()
+    B, N, M = cost.shape
+    dev = cost.device
+    pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
+    with torch.cuda.device(dev):
+        assign = torch.empty((B, N), dtype=torch.int64, device=dev)
+        prices = torch.empty((B, M), dtype=pdt, device=dev)
+        stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
+        status = torch.zeros((1,), dtype=torch.int32, device=dev)
+        code = DTYPE_CODE[cost.dtype]
+        if B == 0 or N == 0:
+            prices.zero_()
+            stats.zero_()
+            return assign, prices, stats, status
+        ws_bytes = lib.ela_auction_workspace_bytes(code, B, N, M, int(path))
+        if ws_bytes == 0:
+            _lib.check(_lib.ELA_ERR_UNSUPPORTED if M >= 2 else _lib.ELA_ERR_ARGUMENT,
+                       f"ela_auction_workspace_bytes(B={B}, N={N}, M={M}, path={path})")
+        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+        e = (ctypes.c_double * len(eps))(*eps)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        rc = lib.ela_auction_solve(
+            ctypes.c_void_p(cost.data_ptr()), code, B, N, M, cost.stride(0), cost.stride(1),
+            e, len(eps), int(max_iter), int(path), ctypes.c_void_p(assign.data_ptr()),
+            ctypes.c_void_p(prices.data_ptr()), ctypes.c_void_p(stats.data_ptr()),
+            ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
+            ctypes.c_void_p(stream))
+        _lib.check(rc, "ela_auction_solve")
+    return assign, prices, stats, status
+
+
+@auction_solve_op.register_fake
+def _(cost, eps, max_iter, path):
+    B, N, M = cost.shape
+    pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
+    return (cost.new_empty((B, N), dtype=torch.int64), cost.new_empty((B, M), dtype=pdt),
+            cost.new_empty((B, 4), dtype=torch.int64), cost.new_empty((1,), dtype=torch.int32))
+
+
+def solve(cost: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path: int = _lib.PATH_AUTO,
+          check: bool = True):
+    """Solve a (B,N,M) or (N,M) CUDA cost tensor.
+
+    epsilon: the reference's constant epsilon, or a schedule (one full solve per
+    value, each starting from the previous prices).
+    Returns (assignment, prices, stats); with ``check`` the device status is read
+    back (one synchronisation) and a device-side error raises AuctionError.
+    """
+    squeeze = cost.dim() == 2
+    if squeeze:
+        cost = cost.unsqueeze(0)
+    if max_iter < 0:
+        raise ValueError("max_iter must be >= 0")
+    sched = _as_schedule(epsilon)
+    if any(not (e > 0.0) or e == float("inf") for e in sched):
+        raise ValueError("every epsilon must be finite and > 0")
+    assign, prices, stats, status = auction_solve_op(cost.detach(), sched, int(max_iter), int(path))
+    if check:
+        st = int(status.item())
+        _lib.check(st, "auction kernel")
+    if squeeze:
+        return assign[0], prices[0], stats[0]
+    return assign, prices, stats
+
+
+class AuctionB200:
+    """Backend plug-in with the reference backend's interface.
+
+    ``AuctionB200(epsilon, max_iter).solve(cost) -> (assignment, prices)``:
+    assignment (B,N) int64, -1 for rows left unassigned after max_iter rounds;
+    prices (B,M) fp32 (fp64 for fp64 input).  Same constructor and return
+    contract as AuctionTorch (torch_backend.py:4-9,158).
+    """
+
+    def __init__(self, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path: int = _lib.PATH_AUTO):
+        self.epsilon = epsilon
+        self.max_iter = max_iter
+        self.path = path
+        self.last_stats = None
+
+    def solve(self, cost_matrix: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        assign, prices, stats = solve(cost_matrix, self.epsilon, self.max_iter, self.path)
+        self.last_stats = stats
+        return assign, prices

@@ -1,0 +1,109 @@
+/*
+ * ela_auction.h -- C ABI of the B200 auction linear-assignment solver
+ * (libela_auction.so, built from efficient-linear-assignment_b200/csrc/ela_auction.cu).
+ *
+ * Plain pointers and sizes only; no torch types.  All pointers passed to the
+ * solve call are DEVICE pointers on the current CUDA device except the epsilon
+ * schedule, which is a host array.  Work is enqueued on `stream` and the call
+ * returns without waiting for it.
+ *
+ * Reference interfaces this ABI replaces (paths inside the reference project):
+ *   - pybind11 solve_auction_cuda(cost, epsilon, max_iter, persistent_mode)
+ *       src/csrc/interface.cpp:4,64 ; src/csrc/kernels.cu:449-585
+ *     -> ela_auction_solve (the whole solve, every round on the device)
+ *   - the backend plug-in AuctionCPPCCUDA.solve(cost) -> (assignment, prices)
+ *       src/efficient_linear_assignment/auction/cpp_backend.py:24-40
+ *     -> reached from Python through the ctypes binding in the package's _lib.py
+ *   - the device scratch the reference allocates inside solve_auction_cuda
+ *       src/csrc/kernels.cu:461-472
+ *     -> caller-owned workspace sized by ela_auction_workspace_bytes
+ */
+#ifndef ELA_AUCTION_H
+#define ELA_AUCTION_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by the calls below and written to *status_out. */
+enum {
+    ELA_OK = 0,
+    ELA_ERR_ARGUMENT = 1,    /* bad size, stride, dtype, schedule or pointer    */
+    ELA_ERR_CUDA = 2,        /* a CUDA runtime call or launch failed             */
+    ELA_ERR_TIMEOUT = 3,     /* a device-side wait ran past its limit            */
+    ELA_ERR_UNSUPPORTED = 4, /* valid arguments this build cannot run (size)     */
+    ELA_ERR_INTERNAL = 5     /* a device-side consistency check failed           */
+};
+
+/* Element type of the cost matrix. */
+enum { ELA_DTYPE_F32 = 0, ELA_DTYPE_F16 = 1, ELA_DTYPE_BF16 = 2, ELA_DTYPE_F64 = 3 };
+
+/* Kernel choice.  AUTO picks by batch and problem size. */
+enum { ELA_PATH_AUTO = 0, ELA_PATH_CTA = 1, ELA_PATH_GRID = 2 };
+
+/* Library ABI version (major*100 + minor). */
+int ela_auction_version(void);
+
+/* Human-readable name of a status code. */
+const char* ela_status_string(int status);
+
+/*
+ * Bytes of device workspace ela_auction_solve needs for these sizes and path
+ * (on the current device).  Returns 0 if the arguments are invalid.
+ */
+size_t ela_auction_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t M, int path);
+
+/*
+ * Solve B independent N x M assignment problems (minimise total cost) with the
+ * Jacobi auction of the reference torch backend
+ * (src/efficient_linear_assignment/auction/torch_backend.py:9-159).
+ *
+ *   cost        device, element (b,i,j) at cost[b*stride_b + i*stride_n + j]
+ *   dtype       ELA_DTYPE_*; fp16/bf16 are widened to fp32, prices and bids are
+ *               fp32 (fp64 for ELA_DTYPE_F64)
+ *   eps_schedule, n_eps
+ *               host array of n_eps >= 1 epsilons, each > 0.  n_eps == 1 is the
+ *               reference's constant-epsilon solve; n_eps > 1 runs one full
+ *               solve per epsilon, each starting from the previous prices
+ *   max_iter    bidding rounds allowed per epsilon (reference default 1000)
+ *   assign_out  device int64[B*N]; column of each row, -1 if unassigned
+ *   prices_out  device float[B*M] (double[B*M] for ELA_DTYPE_F64)
+ *   stats_out   device int64[B*4] or NULL: per problem
+ *               {bidding rounds, row-bids, 0, unassigned rows at exit}
+ *   status_out  device int32[1] or NULL; receives ELA_OK or a device-side error
+ *   workspace   device, >= ela_auction_workspace_bytes(...) bytes, 256-byte aligned
+ *   stream      cudaStream_t (NULL = legacy default stream)
+ *
+ * Requires M >= 2 when N > 0 (top-2 bidding), stride_n >= M, stride_b >= N*stride_n.
+ * Returns ELA_OK once the work is enqueued, or an error code.
+ */
+int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
+                      int64_t stride_b, int64_t stride_n, const double* eps_schedule,
+                      int n_eps, int max_iter, int path, int64_t* assign_out,
+                      void* prices_out, int64_t* stats_out, int32_t* status_out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Limit, in nanoseconds, on every device-side wait of the grid path (the
+ * per-round barrier between the CTAs that share one problem).  A wait that
+ * runs out writes ELA_ERR_TIMEOUT to *status_out and the kernel returns.
+ * Default 2 s.  Process-wide setting.
+ */
+void ela_auction_set_wait_limit_ns(uint64_t ns);
+
+/*
+ * Test hook for the timeout path.  When `on` is nonzero, CTA 0 of every group
+ * of the grid path leaves out its arrival at the first round barrier, so the
+ * other CTAs' bounded wait runs out and the solve ends with ELA_ERR_TIMEOUT
+ * (no fault, no hang; the CUDA context stays usable).  Process-wide setting.
+ */
+void ela_auction_debug_skip_arrive(int on);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ELA_AUCTION_H */

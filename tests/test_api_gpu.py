@@ -1,0 +1,126 @@
+"""GPU tests of the public API, ported from the reference's auction tests
+(tests/test_all.py, tests/test_robustness.py) plus the IMLE backward."""
+import pytest
+import scipy.optimize
+import torch
+
+import efficient_linear_assignment_b200 as ela
+from efficient_linear_assignment_b200 import _lib
+
+pytestmark = pytest.mark.gpu
+dev = "cuda"
+
+
+def total_cost(cost, idx):
+    B, N, _ = cost.shape
+    return cost[torch.arange(B)[:, None], torch.arange(N)[None], idx].sum(1)
+
+
+def test_simple_match_vs_scipy():  # reference tests/test_all.py:19-44
+    cost = ela.workloads.uniform(2, 8, 8, seed=3).to(dev)
+    idx = ela.linear_assignment(cost, epsilon=1e-3, max_iter=2000)
+    for b in range(2):
+        r, c = scipy.optimize.linear_sum_assignment(cost[b].cpu().numpy())
+        assert total_cost(cost[b:b + 1], idx[b:b + 1]).item() <= cost[b].cpu().numpy()[r, c].sum() + 1e-1
+
+
+@pytest.mark.parametrize("N", [128, 136, 144, 256])
+def test_correctness_vs_hungarian(N):  # reference tests/test_robustness.py:10-60
+    cost = ela.workloads.uniform(2, N, N, seed=N).to(dev)
+    idx = ela.linear_assignment(cost, epsilon=1e-3, max_iter=5000)
+    mine = total_cost(cost, idx).cpu()
+    for b in range(2):
+        r, c = scipy.optimize.linear_sum_assignment(cost[b].double().cpu().numpy())
+        opt = cost[b].cpu().numpy()[r, c].sum()
+        assert mine[b].item() - opt <= 1.5 * N * 1e-3
+        assert len(torch.unique(idx[b])) == N
+
+
+def test_degenerate_cases():  # reference tests/test_robustness.py:63-99
+    for cost in (torch.zeros(2, 32, 32, device=dev), torch.full((2, 32, 32), 10.0, device=dev)):
+        idx = ela.linear_assignment(cost, max_iter=1000)
+        for b in range(2):
+            assert len(torch.unique(idx[b])) == 32
+
+
+def test_batched_correctness():  # reference tests/test_robustness.py:101-126
+    cost = torch.rand(4, 32, 32, device=dev)
+    cost[0] = 100.0
+    cost[0].diagonal().zero_()
+    idx = ela.linear_assignment(cost, max_iter=2000)
+    assert torch.equal(idx[0], torch.arange(32, device=dev))
+    for b in range(1, 4):
+        assert len(torch.unique(idx[b])) == 32
+
+
+def test_unbatched_input_and_one_hot():
+    cost = ela.workloads.uniform(1, 64, 64, seed=9)[0].to(dev)
+    idx = ela.linear_assignment(cost, epsilon=1e-3)
+    P = ela.linear_assignment(cost, epsilon=1e-3, return_indices=False)
+    assert idx.shape == (64,) and P.shape == (64, 64)
+    assert torch.equal(P.argmax(1), idx)
+    assert P.dtype == cost.dtype
+
+
+def test_imle_gradient_flows():  # reference tests/test_all.py:46-114
+    cost = torch.randn(1, 8, 8, device=dev, dtype=torch.double, requires_grad=True)
+    out = ela.linear_assignment(cost, epsilon=1e-3, max_iter=200, return_indices=False)
+    (out * cost).sum().backward()
+    assert cost.grad is not None and (cost.grad != 0).any()
+
+
+def test_imle_backward_is_target_minus_forward(oracle_mod):
+    g = torch.Generator().manual_seed(4)
+    C = torch.rand(2, 16, 16, generator=g)
+    G = torch.randn(2, 16, 16, generator=g)
+    c = C.to(dev).requires_grad_(True)
+    P = ela.linear_assignment(c, epsilon=1e-3, return_indices=False)
+    P.backward(G.to(dev))
+    af, _, _ = oracle_mod.solve(C, 1e-3, 1000)
+    at, _, _ = oracle_mod.solve(C + G, 1e-3, 1000)
+    eye = torch.eye(16)
+    expect = eye[at.clamp(min=0)] * (at >= 0)[..., None] - eye[af.clamp(min=0)] * (af >= 0)[..., None]
+    assert torch.equal(c.grad.cpu(), expect)
+
+
+def test_unassigned_rows_map_to_zero():
+    cost = ela.workloads.uniform(1, 16, 8, seed=13).to(dev)
+    a, _, st = ela.solve(cost, 1e-2, 50)
+    idx = ela.linear_assignment(cost, epsilon=1e-2, max_iter=50)
+    assert (a == -1).any()
+    assert torch.equal(idx, a.clamp(min=0))
+
+
+def test_max_iter_zero():
+    cost = torch.rand(2, 16, 16, device=dev)
+    for path in (ela.PATH_CTA, ela.PATH_GRID):
+        a, p, st = ela.solve(cost, 1e-2, 0, path=path)
+        assert (a == -1).all() and (p == 0).all() and (st[:, 3] == 16).all()
+
+
+def test_nondefault_stream():
+    cost = ela.workloads.uniform(3, 128, 128, seed=2).to(dev)
+    ref, _, _ = ela.solve(cost, 1e-2)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        a, _, _ = ela.solve(cost, 1e-2)
+    s.synchronize()
+    assert torch.equal(a, ref)
+
+
+def test_wait_timeout_reports_status_and_context_survives():
+    """A barrier whose arrival never comes ends in ELA_ERR_TIMEOUT, not a hang."""
+    lib = _lib.load()
+    cost = ela.workloads.uniform(1, 512, 512, seed=3).to(dev)
+    lib.ela_auction_set_wait_limit_ns(20_000_000)  # 20 ms
+    lib.ela_auction_debug_skip_arrive(1)
+    try:
+        with pytest.raises(ela.AuctionError) as ei:
+            ela.solve(cost, 1e-2, path=ela.PATH_GRID)
+        assert ei.value.status == _lib.ELA_ERR_TIMEOUT
+    finally:
+        lib.ela_auction_debug_skip_arrive(0)
+        lib.ela_auction_set_wait_limit_ns(2_000_000_000)
+    a, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_GRID)
+    b, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_CTA)
+    assert torch.equal(a, b)

@@ -1,0 +1,51 @@
+"""CPU tests: the oracle against golden vectors recorded from the reference,
+and its column tie rule against torch.topk."""
+import numpy as np
+import pytest
+import torch
+
+from cases import CASES
+from make_golden_io import load_golden, input_digest
+
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_oracle_matches_reference_golden(name, oracle_mod):
+    make, eps, max_iter = CASES[name]
+    cost = make()
+    g = load_golden(name)
+    assert input_digest(cost) == g["digest"], "input generator drifted from the golden recording"
+    a, p, st = oracle_mod.solve(cost, eps, max_iter, nthreads=4)
+    assert np.array_equal(a.numpy(), g["assign"].astype(np.int64))
+    assert np.array_equal(p.numpy(), g["prices"])
+
+
+@pytest.mark.parametrize("M", [2, 3, 5, 8, 16, 40, 96, 120, 127, 128, 129, 256, 1000])
+def test_topk_tie_rule_matches_torch(M, oracle_mod):
+    """A one-row problem is won in round 1 by the column torch.topk(-cost) reports."""
+    torch.set_num_threads(1)
+    g = torch.Generator().manual_seed(M)
+    for trial in range(200):
+        hi = [2, 3, 6][trial % 3]
+        cost = torch.randint(0, hi, (1, 1, M), generator=g).float()
+        a, _, _ = oracle_mod.solve(cost, 0.5, 1)
+        expect = torch.topk(-cost[0], 2, dim=1).indices[0, 0].item()
+        assert a[0, 0].item() == expect, (trial, cost.flatten().tolist())
+
+
+@pytest.mark.parametrize("n", [8, 24, 64])
+def test_c_oracle_equals_numpy_restatement(n, oracle_mod):
+    g = torch.Generator().manual_seed(100 + n)
+    cost = torch.rand(2, n, n, generator=g)
+    a, p, _ = oracle_mod.solve(cost, 1e-3, 500)
+    for b in range(2):
+        a2, p2, tied = oracle_mod.solve_numpy(cost[b].numpy(), 1e-3, 500)
+        if not tied:
+            assert np.array_equal(a[b].numpy(), a2)
+            assert np.array_equal(p[b].numpy(), p2)
+
+
+def test_oracle_threads_do_not_change_results(oracle_mod):
+    cost = CASES["cfg4_head16"][0]()
+    a1, p1, _ = oracle_mod.solve(cost, 1e-2, 1000, nthreads=1)
+    a8, p8, _ = oracle_mod.solve(cost, 1e-2, 1000, nthreads=8)
+    assert torch.equal(a1, a8) and torch.equal(p1, p8)
