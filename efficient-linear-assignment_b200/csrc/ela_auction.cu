@@ -11,14 +11,13 @@
 //   winner  highest row whose |bid - P[j]| < 1e-5                :106-136
 //   owner   the previous owner of a won column becomes unassigned :144-156
 //
-// Two kernels:
-//   auction_cta_kernel   one CTA per problem, all state in shared memory,
-//                        __syncthreads between the phases of a round.
-//   auction_grid_kernel  S CTAs per problem (cooperative launch), one bounded
-//                        barrier per round; the election is settled without a
-//                        second barrier by linking every round's bidders on a
-//                        column into a per-column list that each bidder walks
-//                        after the barrier.
+// One kernel, two layouts of the work:
+//   S == 1   each CTA solves whole problems; all state in shared memory.
+//   S  > 1   S co-resident CTAs share one problem (cooperative launch); every
+//            CTA keeps the full price vector and replays each round's election
+//            from the round's complete bid list, which the CTAs exchange
+//            through tagged words in global memory (the exchange is also the
+//            round's only synchronisation between CTAs).
 // The C ABI is declared in include/ela_auction.h.
 
 #include <cuda_runtime.h>
@@ -33,10 +32,7 @@
 #include "ela_auction.h"
 
 #define ELA_MAX_PHASES 32
-#define ELA_CTA_THREADS 512
-#define ELA_GRID_THREADS 512
 #define ELA_SMALL_M 128           // below this torch.topk uses introselect
-#define ELA_ROWS_PER_CTA_MAX 8192 // owned-row state of the grid path lives in smem
 
 namespace {
 
@@ -305,55 +301,61 @@ struct Params {
     void* prices_out;
     int64_t* stats_out;      // may be null
     int32_t* status;         // never null (points into the workspace if the caller passed none)
-    unsigned char* ws;       // grid path workspace
-    size_t group_bytes;      // grid path: workspace bytes per group
-    int S;                   // grid path: CTAs per problem
-    int ngroups;             // grid path: problems solved at once
-    int rows_per_cta;        // grid path: ceil(N / S)
+    unsigned char* ws;       // workspace: header + exchange segments
+    size_t seg_bytes;        // bytes of one CTA's exchange segment (S > 1)
+    int S;                   // CTAs per problem
+    int ngroups;             // problems in flight (S > 1)
+    int rows_per_cta;        // ceil(N / S)
     unsigned long long wait_ns;
-    int skip_arrive;
+    int skip_publish;        // test hook: CTA 0 never publishes its first round
 };
 
-// --------------------------------------------------------------- one bid
-// The warp computes one row's bid.  Every lane returns the same (j1, bid).
-// scr_v / scr_i: this warp's 128-entry scratch, used only when M < 128.
+// ------------------------------------------------------------ row scanning
+// Top-2 over the columns of one row that this warp covers: the row's 16-byte
+// chunks are dealt to `wpr` warps in turn (warp `sub` takes chunks
+// sub*32+lane, sub*32+lane+32*wpr, ...).  The result is reduced over the warp.
 template <typename In, typename R, int UNROLL>
-__device__ __forceinline__ void bid_row(const Params& p, const In* row, const R* __restrict__ Ps,
-                                        R eps, int lane, R* scr_v, int* scr_i, int& j1_out,
-                                        R& bid_out) {
+__device__ __forceinline__ Top2<R> scan_row(const Params& p, const In* row, const R* __restrict__ Ps,
+                                            int lane, int sub, int wpr) {
     const int M = (int)p.M;
     Top2<R> t;
     top2_init(t);
     if (p.vec_ok) {
         constexpr int W = Elem<In>::W;
         const int nchunks = M / W;
+        const int stride = 32 * wpr;
         const uint4* rv = reinterpret_cast<const uint4*>(row);
-        for (int base = 0; base < nchunks; base += 32 * UNROLL) {
+        for (int base = sub * 32 + lane; base < nchunks; base += stride * UNROLL) {
             uint4 raw[UNROLL];
 #pragma unroll
             for (int u = 0; u < UNROLL; ++u) {
-                const int ch = base + 32 * u + lane;
+                const int ch = base + u * stride;
                 if (ch < nchunks) raw[u] = ld_stream16(rv + ch);
             }
 #pragma unroll
             for (int u = 0; u < UNROLL; ++u) {
-                const int ch = base + 32 * u + lane;
+                const int ch = base + u * stride;
                 if (ch < nchunks) {
                     R x[W];
                     Elem<In>::template unpack<R>(raw[u], x);
 #pragma unroll
-                    for (int e = 0; e < W; ++e) {
-                        const int col = ch * W + e;
-                        top2_add(t, sub_rn(-x[e], Ps[col]), col);
-                    }
+                    for (int e = 0; e < W; ++e) top2_add(t, sub_rn(-x[e], Ps[ch * W + e]), ch * W + e);
                 }
             }
         }
     } else {
-        for (int col = lane; col < M; col += 32)
+        for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
             top2_add(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), col);
     }
-    t = top2_warp(t);
+    return top2_warp(t);
+}
+
+// Column choice and bid from the row's complete top-2 (whole warp, uniform).
+template <typename In, typename R>
+__device__ __forceinline__ void finish_bid(const Params& p, const In* row, const R* __restrict__ Ps,
+                                           const Top2<R>& t, R eps, int lane, R* scr_v, int* scr_i,
+                                           int& j1_out, R& bid_out) {
+    const int M = (int)p.M;
     int j1;
     if (t.v1 == t.v2 && M < ELA_SMALL_M) {
         for (int col = lane; col < M; col += 32) {
@@ -372,368 +374,320 @@ __device__ __forceinline__ void bid_row(const Params& p, const In* row, const R*
     bid_out = add_rn(Ps[j1], add_rn(sub_rn(t.v1, t.v2), eps));
 }
 
-// ======================================================= one CTA per problem
-// Shared-memory layout (byte offsets), identical on host and device.
-struct CtaLayout {
-    size_t win, P, bidval, MB, owner, assign, bidcol, active, scr_v, scr_i, total;
-};
-__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+// ------------------------------------------------------ bid exchange (S > 1)
+// Each CTA of a group publishes its round-t bids in its own segment of the
+// round's buffer (two buffers, by round parity):
+//   word 0                 header  (t+1) << 32 | count
+//   words 1+EW*k ...       entry k: A = (t+1)&0xffff << 48 | row << 24 | col,
+//                          then the bid bits in 32-bit halves, each under a
+//                          32-bit copy of t+1.
+// Every word carries the round tag, so a reader needs no fence: it re-reads
+// any word whose tag is not yet the current round's.  Reading all S segments
+// of round t is also the round's barrier.  A CTA cannot publish round t+2
+// (reusing the buffer) before every CTA has published round t+1, which each
+// does only after it has read all of round t.
+template <typename R> struct Ex;
+template <> struct Ex<float> { static constexpr int EW = 2, INL = 3; };
+template <> struct Ex<double> { static constexpr int EW = 3, INL = 2; };
 
-template <typename R>
-__host__ __device__ inline CtaLayout cta_layout(int64_t N, int64_t M, int warps) {
-    typedef typename std::conditional<sizeof(R) == 4, unsigned int, unsigned long long>::type U;
-    CtaLayout L;
-    size_t o = 0;
-    L.win = o;    o = align_up(o + 8 * (size_t)M, 16);
-    L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);
-    L.bidval = o; o = align_up(o + sizeof(R) * (size_t)N, 16);
-    L.MB = o;     o = align_up(o + sizeof(U) * (size_t)M, 16);
-    L.owner = o;  o = align_up(o + 4 * (size_t)M, 16);
-    L.assign = o; o = align_up(o + 4 * (size_t)N, 16);
-    L.bidcol = o; o = align_up(o + 4 * (size_t)N, 16);
-    L.active = o; o = align_up(o + 4 * (size_t)N, 16);
-    const size_t scr = (M < ELA_SMALL_M) ? (size_t)warps * ELA_SMALL_M : 0;
-    L.scr_v = o;  o = align_up(o + sizeof(R) * scr, 16);
-    L.scr_i = o;  o = align_up(o + 4 * scr, 16);
-    L.total = o;
-    return L;
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* ptr) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
+    return v;
 }
-
-template <typename In, typename R>
-__global__ void __launch_bounds__(ELA_CTA_THREADS)
-auction_cta_kernel(const Params p) {
-    typedef Bits<R> BT;
-    typedef typename BT::U U;
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int s_nact;
-    __shared__ int s_unassigned;
-
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int N = (int)p.N, M = (int)p.M;
-    const CtaLayout L = cta_layout<R>(N, M, nw);
-    unsigned long long* win = reinterpret_cast<unsigned long long*>(smem + L.win);
-    R* P = reinterpret_cast<R*>(smem + L.P);
-    R* bidval = reinterpret_cast<R*>(smem + L.bidval);
-    U* MB = reinterpret_cast<U*>(smem + L.MB);
-    int* owner = reinterpret_cast<int*>(smem + L.owner);
-    int* assign = reinterpret_cast<int*>(smem + L.assign);
-    int* bidcol = reinterpret_cast<int*>(smem + L.bidcol);
-    int* active = reinterpret_cast<int*>(smem + L.active);
-    R* scr_v = reinterpret_cast<R*>(smem + L.scr_v) + warp * ELA_SMALL_M;
-    int* scr_i = reinterpret_cast<int*>(smem + L.scr_i) + warp * ELA_SMALL_M;
-    const R tol = (R)1e-5;
-
-    for (int64_t b = blockIdx.x; b < p.B; b += gridDim.x) {
-        const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
-        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; MB[j] = 0; win[j] = 0ull; }
-        long long rounds = 0, rowbids = 0;
-        unsigned int tag = 0;
-        for (int ph = 0; ph < p.n_eps; ++ph) {
-            const R eps = (R)p.eps[ph];
-            for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
-            for (int i = tid; i < N; i += blockDim.x) assign[i] = -1;
-            __syncthreads();
-            for (int it = 0; it < p.max_iter; ++it) {
-                // 1. active rows (order does not matter: the election below is
-                //    by row id, and each row's bid depends only on its own row)
-                if (tid == 0) s_nact = 0;
-                __syncthreads();
-                for (int i = tid; i < N; i += blockDim.x)
-                    if (assign[i] < 0) active[atomicAdd(&s_nact, 1)] = i;
-                __syncthreads();
-                const int K = s_nact;
-                if (K == 0) break;
-                rounds++;
-                rowbids += K;
-                ++tag;
-                // 2. bids against the round-start prices; column max of the bids
-                for (int k = warp; k < K; k += nw) {
-                    int j1;
-                    R bid;
-                    bid_row<In, R, 4>(p, base + (int64_t)active[k] * p.stride_n, P, eps, lane,
-                                      scr_v, scr_i, j1, bid);
-                    if (lane == 0) {
-                        bidcol[k] = j1;
-                        bidval[k] = bid;
-                        atomicMax(&MB[j1], BT::to(bid));
-                    }
-                }
-                __syncthreads();
-                // 3. election: highest row within 1e-5 of the new price
-                for (int k = tid; k < K; k += blockDim.x) {
-                    const int j = bidcol[k];
-                    if (absval(sub_rn(bidval[k], BT::from(MB[j]))) < tol)
-                        atomicMax(&win[j], ((unsigned long long)tag << 32) | (unsigned int)active[k]);
-                }
-                __syncthreads();
-                // 4. winners take their columns; previous owners drop out
-                for (int k = tid; k < K; k += blockDim.x) {
-                    const int j = bidcol[k], i = active[k];
-                    if (win[j] == (((unsigned long long)tag << 32) | (unsigned int)i)) {
-                        const int prev = owner[j];
-                        if (prev >= 0) assign[prev] = -1;
-                        owner[j] = i;
-                        assign[i] = j;
-                        P[j] = BT::from(MB[j]);
-                        MB[j] = 0;
-                    }
-                }
-                __syncthreads();
-            }
-        }
-        // outputs
-        if (tid == 0) s_unassigned = 0;
-        __syncthreads();
-        int mine = 0;
-        for (int i = tid; i < N; i += blockDim.x) {
-            const int a = assign[i];
-            p.assign_out[b * p.N + i] = a;
-            mine += (a < 0);
-        }
-        if (mine) atomicAdd(&s_unassigned, mine);
-        R* pout = reinterpret_cast<R*>(p.prices_out) + b * p.M;
-        for (int j = tid; j < M; j += blockDim.x) pout[j] = P[j];
-        __syncthreads();
-        if (tid == 0 && p.stats_out) {
-            p.stats_out[4 * b + 0] = rounds;
-            p.stats_out[4 * b + 1] = rowbids;
-            p.stats_out[4 * b + 2] = 0;
-            p.stats_out[4 * b + 3] = s_unassigned;
-        }
-        __syncthreads();
-    }
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* ptr, unsigned long long v) {
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }
-
-// ================================================== S CTAs per problem (grid)
-// Per-group workspace (global memory), byte offsets from the group base:
-//   ctrl   [256]     bar (u32) at 0, cnt[3] (u32) at 128
-//   MB     [3][M]    column max bid of a round, bits (0 = no bid); round t uses t%3
-//   head   [2][M]    u64 (t+1)<<32 | row: last bidder linked on the column in round t
-//   nbid   [2][N]    bid of row i in round t (parity t&1)
-//   nnext  [2][N]    next bidder on the same column in round t, -1 = end
-// A round's buffers are written in round t, read in round t+1 and rewritten
-// no earlier than round t+2 (t+3 for MB/cnt, which are zeroed in round t+2),
-// so a CTA that runs ahead never overwrites data a slower CTA still reads.
-struct GroupLayout {
-    size_t ctrl, MB, head, nbid, nnext, total;
-};
-template <typename R> __host__ __device__ inline GroupLayout group_layout(int64_t N, int64_t M) {
-    GroupLayout L;
-    size_t o = 0;
-    L.ctrl = o;  o += 256;
-    L.MB = o;    o = align_up(o + 3 * sizeof(R) * (size_t)M, 256);
-    L.head = o;  o = align_up(o + 2 * 8 * (size_t)M, 256);
-    L.nbid = o;  o = align_up(o + 2 * sizeof(R) * (size_t)N, 256);
-    L.nnext = o; o = align_up(o + 2 * 4 * (size_t)N, 256);
-    L.total = o;
-    return L;
-}
-// workspace = [256 B launch control: abort flag, status] + ngroups * group bytes
-#define ELA_WS_HEADER 256
-
-struct GridSmem {
-    size_t P, rowcol, rowbid, active, scr_v, scr_i, total;
-};
-template <typename R> __host__ __device__ inline GridSmem grid_smem(int64_t M, int rpc, int warps) {
-    GridSmem L;
-    size_t o = 0;
-    L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);
-    L.rowcol = o; o = align_up(o + 4 * (size_t)rpc, 16);
-    L.rowbid = o; o = align_up(o + 4 * (size_t)rpc, 16);
-    L.active = o; o = align_up(o + 4 * (size_t)rpc, 16);
-    const size_t scr = (M < ELA_SMALL_M) ? (size_t)warps * ELA_SMALL_M : 0;
-    L.scr_v = o;  o = align_up(o + sizeof(R) * scr, 16);
-    L.scr_i = o;  o = align_up(o + 4 * scr, 16);
-    L.total = o;
-    return L;
-}
-
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* p) {
-    unsigned int v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-__device__ __forceinline__ void red_release_add(unsigned int* p, unsigned int v) {
-    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+
+template <typename R>
+__device__ __forceinline__ void put_entry(unsigned long long* seg, int k, unsigned int t1, int row, int col, R bid) {
+    unsigned long long* w = seg + 1 + Ex<R>::EW * k;
+    const unsigned long long tag = (unsigned long long)t1 << 32;
+    st_relaxed_u64(w, ((unsigned long long)(t1 & 0xffffu) << 48) | ((unsigned long long)row << 24) | (unsigned long long)col);
+    const unsigned long long bits = (unsigned long long)Bits<R>::to(bid);
+    st_relaxed_u64(w + 1, tag | (bits & 0xffffffffull));
+    if (Ex<R>::EW == 3) st_relaxed_u64(w + 2, tag | (bits >> 32));
 }
 
-// Barrier of the S CTAs of one group.  The counter only grows; CTA c waits
-// until it reaches `target` (S more per round).  Every wait is bounded: past
-// p.wait_ns the waiter raises the launch-wide abort flag and records
-// ELA_ERR_TIMEOUT; any waiter that sees the flag gives up too.  Returns false
-// when the caller must leave the kernel.
-__device__ __forceinline__ bool group_barrier(const Params& p, unsigned int* bar, unsigned int target,
-                                              int* abort_flag, bool skip_arrive) {
-    __shared__ int s_ok;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int ok = 1;
-        __threadfence();
-        if (!skip_arrive) red_release_add(bar, 1u);
-        const unsigned long long t0 = globaltimer_ns();
-        unsigned int spins = 0;
-        for (;;) {
-            const unsigned int v = ld_acquire_u32(bar);
-            if ((int)(v - target) >= 0) break;
-            if ((++spins & 63u) == 0) {
-                if (*(volatile int*)abort_flag) { ok = 0; break; }
-                if (globaltimer_ns() - t0 > p.wait_ns) {
-                    atomicExch(abort_flag, 1);
-                    atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
-                    ok = 0;
-                    break;
-                }
-            }
-        }
-        __threadfence();
-        s_ok = ok;
-    }
-    __syncthreads();
-    return s_ok != 0;
+// One attempt to read entry k; false if some word is not yet from round t1.
+template <typename R>
+__device__ __forceinline__ bool get_entry(const unsigned long long* seg, int k, unsigned int t1, int& row, int& col,
+                                          R& bid) {
+    const unsigned long long* w = seg + 1 + Ex<R>::EW * k;
+    const unsigned long long a = ld_relaxed_u64(w);
+    const unsigned long long lo = ld_relaxed_u64(w + 1);
+    const unsigned long long hi = (Ex<R>::EW == 3) ? ld_relaxed_u64(w + 2) : 0ull;
+    if ((a >> 48) != (t1 & 0xffffu) || (unsigned int)(lo >> 32) != t1) return false;
+    if (Ex<R>::EW == 3 && (unsigned int)(hi >> 32) != t1) return false;
+    row = (int)((a >> 24) & 0xffffffull);
+    col = (int)(a & 0xffffffull);
+    const unsigned long long bits = (lo & 0xffffffffull) | ((hi & 0xffffffffull) << 32);
+    bid = Bits<R>::from((typename Bits<R>::U)bits);
+    return true;
 }
 
-template <typename In, typename R>
-__global__ void __launch_bounds__(ELA_GRID_THREADS, 1)
-auction_grid_kernel(const Params p) {
+// ================================================================== kernel
+// Shared-memory layout (byte offsets), identical on host and device.
+struct KLayout {
+    size_t P, maxb, win, lbid, lrow, lcol, rowcol, rowbid, active, wtop, scr_v, scr_i, total;
+};
+__host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+template <typename R>
+__host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int warps) {
+    KLayout L;
+    size_t o = 0;
+    L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);   // prices
+    L.maxb = o;   o = align_up(o + sizeof(R) * (size_t)M, 16);   // round's column max bid (bits)
+    L.win = o;    o = align_up(o + 4 * (size_t)M, 16);           // round's elected row + 1
+    L.lbid = o;   o = align_up(o + sizeof(R) * (size_t)N, 16);   // round's bids: value
+    L.lrow = o;   o = align_up(o + 4 * (size_t)N, 16);           //               row
+    L.lcol = o;   o = align_up(o + 4 * (size_t)N, 16);           //               column
+    L.rowcol = o; o = align_up(o + 4 * (size_t)rpc, 16);         // own rows: assigned column or -1
+    L.rowbid = o; o = align_up(o + 4 * (size_t)rpc, 16);         // own rows: column bid on, or -1
+    L.active = o; o = align_up(o + 4 * (size_t)rpc, 16);         // own rows bidding this round
+    L.wtop = o;   o = align_up(o + (2 * sizeof(R) + 8) * (size_t)warps, 16);  // per-warp top-2
+    const size_t scr = (M < ELA_SMALL_M) ? (size_t)warps * ELA_SMALL_M : 0;
+    L.scr_v = o;  o = align_up(o + sizeof(R) * scr, 16);
+    L.scr_i = o;  o = align_up(o + 4 * scr, 16);
+    L.total = o;
+    return L;
+}
+
+// Launch shapes: one CTA per problem runs 256 threads at up to 4 CTAs per SM
+// (a batch of small problems stays in one wave); the multi-CTA path runs 512
+// threads, one CTA per SM.
+#define ELA_THREADS_ONE 256
+#define ELA_MINB_ONE 4
+#define ELA_UNROLL_ONE 4
+#define ELA_THREADS_MULTI 512
+#define ELA_MINB_MULTI 1
+#define ELA_UNROLL_MULTI 8
+#define ELA_MAX_S 256
+#define ELA_WS_HEADER 256
+
+// Round: active rows bid -> bids gathered -> column max (new price) -> highest
+// row within 1e-5 of it wins -> owners of bid-on columns are evicted.
+//   MULTI == false: every CTA solves whole problems (blockIdx.x, +gridDim.x, ...);
+//                   a round's bids go straight into the CTA's shared list.
+//   MULTI == true:  S CTAs share a problem; CTA c owns rows c, c+S, c+2S, ...
+template <typename In, typename R, bool MULTI, int THREADS, int MINB, int UNROLL>
+__global__ void __launch_bounds__(THREADS, MINB)
+auction_kernel(const Params p) {
     typedef Bits<R> BT;
     typedef typename BT::U U;
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int s_nact, s_unassigned;
-    __shared__ unsigned int s_kprev;
-    __shared__ int s_err;
+    __shared__ int s_nact, s_total, s_extra, s_fail;
+    __shared__ int s_cnt[MULTI ? ELA_MAX_S : 1], s_off[MULTI ? ELA_MAX_S : 1];
+    __shared__ int s_unassigned;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int S = p.S, g = blockIdx.x / S, c = blockIdx.x % S;
-    if (g >= p.ngroups) return;
-    const int N = (int)p.N, M = (int)p.M, rpc = p.rows_per_cta;
-    const int my_rows = (c < N) ? (N - 1 - c) / S + 1 : 0;  // rows c, c+S, c+2S, ...
-
-    const GridSmem SL = grid_smem<R>(M, rpc, nw);
-    R* Ps = reinterpret_cast<R*>(smem + SL.P);
-    int* rowcol = reinterpret_cast<int*>(smem + SL.rowcol);  // assigned column or -1
-    int* rowbid = reinterpret_cast<int*>(smem + SL.rowbid);  // column bid on last round or -1
-    int* active = reinterpret_cast<int*>(smem + SL.active);
-    R* scr_v = reinterpret_cast<R*>(smem + SL.scr_v) + warp * ELA_SMALL_M;
-    int* scr_i = reinterpret_cast<int*>(smem + SL.scr_i) + warp * ELA_SMALL_M;
-
-    int* abort_flag = reinterpret_cast<int*>(p.ws);
-    const GroupLayout GL = group_layout<R>(N, M);
-    unsigned char* gb = p.ws + ELA_WS_HEADER + (size_t)g * p.group_bytes;
-    unsigned int* bar = reinterpret_cast<unsigned int*>(gb + GL.ctrl);
-    unsigned int* cnt = reinterpret_cast<unsigned int*>(gb + GL.ctrl + 128);
-    U* MBa = reinterpret_cast<U*>(gb + GL.MB);
-    unsigned long long* heada = reinterpret_cast<unsigned long long*>(gb + GL.head);
-    R* nbida = reinterpret_cast<R*>(gb + GL.nbid);
-    int* nnexta = reinterpret_cast<int*>(gb + GL.nnext);
+    const int S = MULTI ? p.S : 1;
+    const int g = blockIdx.x / S, c = blockIdx.x % S;
+    const int N = (int)p.N, M = (int)p.M;
+    const int my_rows = (c < N) ? (N - 1 - c) / S + 1 : 0;  // rows c, c+S, ...
+    const KLayout L = k_layout<R>(N, M, p.rows_per_cta, nw);
+    R* P = reinterpret_cast<R*>(smem + L.P);
+    U* maxb = reinterpret_cast<U*>(smem + L.maxb);
+    int* win = reinterpret_cast<int*>(smem + L.win);
+    R* lbid = reinterpret_cast<R*>(smem + L.lbid);
+    int* lrow = reinterpret_cast<int*>(smem + L.lrow);
+    int* lcol = reinterpret_cast<int*>(smem + L.lcol);
+    int* rowcol = reinterpret_cast<int*>(smem + L.rowcol);
+    int* rowbid = reinterpret_cast<int*>(smem + L.rowbid);
+    int* active = reinterpret_cast<int*>(smem + L.active);
+    Top2<R>* wtop = reinterpret_cast<Top2<R>*>(smem + L.wtop);
+    R* scr_v = reinterpret_cast<R*>(smem + L.scr_v) + warp * ELA_SMALL_M;
+    int* scr_i = reinterpret_cast<int*>(smem + L.scr_i) + warp * ELA_SMALL_M;
     const R tol = (R)1e-5;
 
-    unsigned int t = 0;        // round tag, identical in all CTAs of the group
-    unsigned int target = 0;   // barrier target
-    bool first_barrier = true;
-    if (tid == 0) s_err = 0;
+    int* abort_flag = reinterpret_cast<int*>(p.ws);
+    unsigned char* gbase = p.ws + ELA_WS_HEADER + (size_t)g * 2 * S * p.seg_bytes;
 
-    for (int64_t b = g; b < p.B; b += p.ngroups) {
+    const int nprob_step = MULTI ? p.ngroups : gridDim.x;
+    unsigned int t = 0;  // round counter, identical in all CTAs of a group
+    bool first_publish = true;
+
+    for (int64_t b = MULTI ? g : blockIdx.x; b < p.B; b += nprob_step) {
         const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
-        for (int j = tid; j < M; j += blockDim.x) Ps[j] = (R)0;
+        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; maxb[j] = 0; win[j] = 0; }
         for (int q = tid; q < my_rows; q += blockDim.x) { rowcol[q] = -1; rowbid[q] = -1; }
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
-        bool first = true;
         __syncthreads();
-        if (p.max_iter > 0) {
-            for (;;) {
-                if (!first) {
-                    // ---- apply round t-1: elections, evictions, prices
-                    const unsigned int tp = t - 1;
-                    const U* MBp = MBa + (size_t)(tp % 3) * M;
-                    const unsigned long long* headp = heada + (size_t)(tp & 1) * M;
-                    const R* nbidp = nbida + (size_t)(tp & 1) * N;
-                    const int* nnextp = nnexta + (size_t)(tp & 1) * N;
-                    for (int q = tid; q < my_rows; q += blockDim.x) {
-                        const int i = c + q * S;
-                        const int jb = rowbid[q];
-                        if (jb >= 0) {
-                            rowbid[q] = -1;
-                            const unsigned long long h = __ldcg(headp + jb);
-                            const R mb = BT::from(__ldcg(MBp + jb));
-                            if ((unsigned int)(h >> 32) != t) { s_err = ELA_ERR_INTERNAL; continue; }
-                            int cur = (int)(unsigned int)(h & 0xffffffffull), best = -1, steps = 0;
-                            while (cur >= 0 && cur < N && steps <= N) {
-                                const R bc = __ldcg(nbidp + cur);
-                                const int nx = __ldcg(nnextp + cur);
-                                if (cur > best && absval(sub_rn(bc, mb)) < tol) best = cur;
-                                cur = nx;
-                                ++steps;
-                            }
-                            if (steps > N || cur >= N) s_err = ELA_ERR_INTERNAL;
-                            if (best == i) rowcol[q] = jb;
-                        } else {
-                            const int j = rowcol[q];
-                            if (j >= 0 && (unsigned int)(__ldcg(headp + j) >> 32) == t) rowcol[q] = -1;
+        while (ph < p.n_eps) {
+            if (it == p.max_iter) {  // round budget of this epsilon used up
+                if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
+                    for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
+                it = 0;
+                __syncthreads();
+                continue;
+            }
+            const R eps = (R)p.eps[ph];
+            const unsigned int t1 = t + 1;
+            // ---- own rows that bid this round
+            if (tid == 0) { s_nact = 0; s_total = 0; s_extra = 0; s_fail = 0; }
+            __syncthreads();
+            for (int q = tid; q < my_rows; q += blockDim.x)
+                if (rowcol[q] < 0) active[atomicAdd(&s_nact, 1)] = q;
+            __syncthreads();
+            const int K = s_nact;
+            unsigned long long* myseg =
+                reinterpret_cast<unsigned long long*>(gbase + (size_t)((t & 1) * S + c) * p.seg_bytes);
+            // ---- bids against the round-start prices.  With few rows, a row is
+            //      dealt to several warps so that its scan is one memory latency.
+            if (K > 0) {
+                int wpr = 1;
+                if (M >= 1024 && K < nw) {
+                    wpr = nw / K;
+                    while (wpr & (wpr - 1)) wpr &= wpr - 1;  // power of two
+                }
+                const int groups = nw / wpr;
+                for (int kb = 0; kb < K; kb += groups) {
+                    const int k = kb + warp / wpr, sub = warp % wpr;
+                    const bool has = k < K;
+                    const int q = has ? active[k] : 0;
+                    const int i = c + q * S;
+                    const In* row = base + (int64_t)i * p.stride_n;
+                    Top2<R> tt;
+                    top2_init(tt);
+                    if (has) tt = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                    if (wpr > 1) {
+                        if (has && lane == 0) wtop[warp] = tt;
+                        __syncthreads();
+                        if (has && sub == 0)
+                            for (int w = 1; w < wpr; ++w) tt = top2_merge(tt, wtop[warp + w]);
+                    }
+                    if (has && sub == 0) {
+                        int j1;
+                        R bid;
+                        finish_bid<In, R>(p, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
+                        if (lane == 0) {
+                            rowbid[q] = j1;
+                            if (!MULTI) { lbid[k] = bid; lrow[k] = i; lcol[k] = j1; }
+                            else put_entry<R>(myseg, k, t1, i, j1, bid);
                         }
                     }
-                    for (int j = tid; j < M; j += blockDim.x) {
-                        const U u = __ldcg(MBp + j);
-                        if (u) Ps[j] = BT::from(u);
-                    }
-                    if (tid == 0) s_kprev = __ldcg(cnt + (tp % 3));
-                    __syncthreads();
-                    const unsigned int kprev = s_kprev;
-                    if (kprev > 0) { rounds++; rowbids += kprev; }
-                    if (kprev == 0 || it == p.max_iter) {
-                        if (++ph == p.n_eps) break;
-                        it = 0;
-                        for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
-                    }
+                    if (wpr > 1) __syncthreads();
                 }
-                first = false;
-                const R eps = (R)p.eps[ph];
-                // ---- zero round t+1's column maxima and counter
-                {
-                    U* MBn = MBa + (size_t)((t + 1) % 3) * M;
-                    for (int j = c * blockDim.x + tid; j < M; j += S * blockDim.x) MBn[j] = 0;
-                    if (c == 0 && tid == 0) cnt[(t + 1) % 3] = 0u;
-                }
-                // ---- bid
-                if (tid == 0) s_nact = 0;
-                __syncthreads();
-                for (int q = tid; q < my_rows; q += blockDim.x)
-                    if (rowcol[q] < 0) active[atomicAdd(&s_nact, 1)] = q;
-                __syncthreads();
-                const int K = s_nact;
-                U* MBc = MBa + (size_t)(t % 3) * M;
-                unsigned long long* headc = heada + (size_t)(t & 1) * M;
-                R* nbidc = nbida + (size_t)(t & 1) * N;
-                int* nnextc = nnexta + (size_t)(t & 1) * N;
-                for (int k = warp; k < K; k += nw) {
-                    const int q = active[k];
-                    const int i = c + q * S;
-                    int j1;
-                    R bid;
-                    bid_row<In, R, 8>(p, base + (int64_t)i * p.stride_n, Ps, eps, lane, scr_v, scr_i, j1, bid);
-                    if (lane == 0) {
-                        atomicMax(MBc + j1, BT::to(bid));
-                        const unsigned long long old =
-                            atomicExch(headc + j1, ((unsigned long long)(t + 1) << 32) | (unsigned int)i);
-                        const int nx = ((unsigned int)(old >> 32) == t + 1) ? (int)(unsigned int)(old & 0xffffffffull) : -1;
-                        __stcg(nbidc + i, bid);
-                        __stcg(nnextc + i, nx);
-                        rowbid[q] = j1;
-                    }
-                }
-                if (tid == 0 && K > 0) atomicAdd(cnt + (t % 3), (unsigned int)K);
-                ++it;
-                target += S;
-                const bool skip = p.skip_arrive && first_barrier && c == 0;
-                first_barrier = false;
-                if (!group_barrier(p, bar, target, abort_flag, skip)) return;
-                ++t;
             }
+            __syncthreads();
+            // ---- gather the round's bids of the whole problem
+            int ntot;
+            if (!MULTI) {
+                ntot = K;
+            } else {
+                if (tid == 0 && !(p.skip_publish && first_publish && c == 0))
+                    st_relaxed_u64(myseg, ((unsigned long long)t1 << 32) | (unsigned int)K);
+                first_publish = false;
+                if (tid < S) {
+                    const unsigned long long* seg =
+                        reinterpret_cast<const unsigned long long*>(gbase + (size_t)((t & 1) * S + tid) * p.seg_bytes);
+                    const unsigned long long t0 = globaltimer_ns();
+                    unsigned int spins = 0;
+                    int cntv = -1;
+                    for (;;) {  // bounded wait for the segment's header
+                        const unsigned long long h = ld_relaxed_u64(seg);
+                        if ((unsigned int)(h >> 32) == t1) { cntv = (int)(unsigned int)(h & 0xffffffffull); break; }
+                        if ((++spins & 15u) == 0) {
+                            if (*(volatile int*)abort_flag) break;
+                            if (globaltimer_ns() - t0 > p.wait_ns) {
+                                atomicExch(abort_flag, 1);
+                                atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                                break;
+                            }
+                        }
+                    }
+                    if (cntv < 0) {
+                        s_fail = 1;
+                    } else {
+                        const int off = atomicAdd(&s_total, cntv);
+                        s_cnt[tid] = cntv;
+                        s_off[tid] = off;
+                        if (cntv > Ex<R>::INL) s_extra = 1;
+                        const int ninl = cntv < Ex<R>::INL ? cntv : Ex<R>::INL;
+                        for (int k = 0; k < ninl; ++k) {
+                            int rr = 0, cc = 0;
+                            R bb = (R)0;
+                            unsigned int tries = 0;
+                            while (!get_entry<R>(seg, k, t1, rr, cc, bb)) {
+                                if (++tries > (1u << 22)) {
+                                    s_fail = 1;
+                                    atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                                    atomicExch(abort_flag, 1);
+                                    break;
+                                }
+                            }
+                            lbid[off + k] = bb; lrow[off + k] = rr; lcol[off + k] = cc;
+                        }
+                    }
+                }
+                __syncthreads();
+                if (s_fail) return;
+                if (s_extra) {  // rounds with many bids: read the remaining entries together
+                    for (int sg = 0; sg < S; ++sg) {
+                        const int cn = s_cnt[sg];
+                        if (cn <= Ex<R>::INL) continue;
+                        const unsigned long long* seg =
+                            reinterpret_cast<const unsigned long long*>(gbase + (size_t)((t & 1) * S + sg) * p.seg_bytes);
+                        for (int k = Ex<R>::INL + tid; k < cn; k += blockDim.x) {
+                            int rr = 0, cc = 0;
+                            R bb = (R)0;
+                            unsigned int tries = 0;
+                            while (!get_entry<R>(seg, k, t1, rr, cc, bb)) {
+                                if (++tries > (1u << 22)) {
+                                    s_fail = 1;
+                                    atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                                    atomicExch(abort_flag, 1);
+                                    break;
+                                }
+                            }
+                            lbid[s_off[sg] + k] = bb; lrow[s_off[sg] + k] = rr; lcol[s_off[sg] + k] = cc;
+                        }
+                    }
+                    __syncthreads();
+                    if (s_fail) return;
+                }
+                ntot = s_total;
+            }
+            ++t;
+            if (ntot == 0) {  // nobody bid: this epsilon's solve has converged
+                if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
+                    for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
+                it = 0;
+                __syncthreads();
+                continue;
+            }
+            rounds++;
+            rowbids += ntot;
+            // ---- election, identical in every CTA of the group
+            for (int e = tid; e < ntot; e += blockDim.x) atomicMax(&maxb[lcol[e]], BT::to(lbid[e]));
+            __syncthreads();
+            for (int e = tid; e < ntot; e += blockDim.x) {
+                const int j = lcol[e];
+                if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[e] + 1);
+            }
+            __syncthreads();
+            for (int q = tid; q < my_rows; q += blockDim.x) {
+                const int jb = rowbid[q];
+                if (jb >= 0) {
+                    rowcol[q] = (win[jb] == c + q * S + 1) ? jb : -1;
+                    rowbid[q] = -1;
+                } else {
+                    const int j = rowcol[q];
+                    if (j >= 0 && maxb[j] != 0) rowcol[q] = -1;  // someone took the column
+                }
+            }
+            for (int e = tid; e < ntot; e += blockDim.x) P[lcol[e]] = BT::from(maxb[lcol[e]]);
+            __syncthreads();
+            for (int e = tid; e < ntot; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
+            ++it;
+            __syncthreads();
         }
         // ---- outputs of problem b
         if (tid == 0) s_unassigned = 0;
@@ -745,22 +699,22 @@ auction_grid_kernel(const Params p) {
             mine += (a < 0);
         }
         if (mine) atomicAdd(&s_unassigned, mine);
+        if (c == 0) {
+            R* pout = reinterpret_cast<R*>(p.prices_out) + b * p.M;
+            for (int j = tid; j < M; j += blockDim.x) pout[j] = P[j];
+        }
         __syncthreads();
         if (tid == 0 && p.stats_out) {
-            if (s_unassigned) atomicAdd(reinterpret_cast<unsigned long long*>(p.stats_out + 4 * b + 3),
-                                        (unsigned long long)s_unassigned);
+            if (s_unassigned)
+                atomicAdd(reinterpret_cast<unsigned long long*>(p.stats_out + 4 * b + 3),
+                          (unsigned long long)s_unassigned);
             if (c == 0) {
                 p.stats_out[4 * b + 0] = rounds;
                 p.stats_out[4 * b + 1] = rowbids;
             }
         }
-        if (c == 0) {
-            R* pout = reinterpret_cast<R*>(p.prices_out) + b * p.M;
-            for (int j = tid; j < M; j += blockDim.x) pout[j] = Ps[j];
-        }
         __syncthreads();
     }
-    if (tid == 0 && s_err) atomicCAS(p.status, ELA_OK, s_err);
 }
 
 }  // namespace
@@ -769,14 +723,13 @@ auction_grid_kernel(const Params p) {
 namespace {
 
 unsigned long long g_wait_ns = 2000000000ull;
-int g_skip_arrive = 0;
+int g_skip_publish = 0;
 
 struct Plan {
-    int path;            // ELA_PATH_CTA or ELA_PATH_GRID
-    int S, ngroups, rpc; // grid path
-    size_t smem;         // dynamic shared memory per CTA
-    size_t group_bytes;  // grid path
-    size_t ws_bytes;     // total workspace
+    int S, ngroups, rpc;
+    size_t smem;       // dynamic shared memory per CTA
+    size_t seg_bytes;  // S > 1
+    size_t ws_bytes;   // total workspace
 };
 
 int elem_size(int dtype) {
@@ -789,42 +742,50 @@ int elem_size(int dtype) {
     }
 }
 
+// CTAs per problem on the multi-CTA path: all SMs shared evenly by the
+// problems in flight, optionally capped by ELA_CTAS_PER_PROBLEM (tuning knob).
+int ctas_per_problem(int64_t B, int64_t N, int sms, int& ngroups) {
+    ngroups = (int)(B < sms ? B : sms);
+    if (ngroups < 1) ngroups = 1;
+    int S = sms / ngroups;
+    if (const char* env = getenv("ELA_CTAS_PER_PROBLEM")) {
+        const int cap = atoi(env);
+        if (cap >= 2 && cap < S) S = cap;
+    }
+    if (S > ELA_MAX_S) S = ELA_MAX_S;
+    if (S > N) S = (int)N;
+    return S < 2 ? 2 : S;
+}
+
 template <typename R>
 int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_max, Plan& pl) {
-    const int warps = ELA_CTA_THREADS / 32;
-    const size_t cta_smem = cta_layout<R>(N, M, warps).total;
-    const bool cta_fits = cta_smem <= smem_max;
-    // grid plan
-    const int T = sms;  // one CTA per SM
-    int ngroups = (int)(B < T ? B : T);
-    if (ngroups < 1) ngroups = 1;
-    int S = T / ngroups;
-    if (S > N) S = (int)(N > 0 ? N : 1);
-    if (S < 1) S = 1;
+    const size_t one_smem = k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32).total;
+    const bool one_fits = one_smem <= smem_max;
+    int ngroups = 1;
+    const int S = ctas_per_problem(B, N, sms, ngroups);
     const int rpc = (int)((N + S - 1) / S);
-    const size_t grid_smem_b = grid_smem<R>(M, rpc, ELA_GRID_THREADS / 32).total;
-    const bool grid_fits = rpc <= ELA_ROWS_PER_CTA_MAX && grid_smem_b <= smem_max;
+    const size_t multi_smem = k_layout<R>(N, M, rpc, ELA_THREADS_MULTI / 32).total;
+    const bool multi_fits = multi_smem <= smem_max && N < (1 << 24) && M < (1 << 24) && N >= 2;
 
     int chosen = path;
     if (path == ELA_PATH_AUTO) {
-        if (cta_fits && (N <= 512 || B >= sms)) chosen = ELA_PATH_CTA;
-        else if (grid_fits) chosen = ELA_PATH_GRID;
-        else if (cta_fits) chosen = ELA_PATH_CTA;
+        if (one_fits && (N <= 512 || B >= sms)) chosen = ELA_PATH_CTA;
+        else if (multi_fits) chosen = ELA_PATH_GRID;
+        else if (one_fits) chosen = ELA_PATH_CTA;
         else return ELA_ERR_UNSUPPORTED;
     }
-    pl.path = chosen;
     if (chosen == ELA_PATH_CTA) {
-        if (!cta_fits) return ELA_ERR_UNSUPPORTED;
-        pl.S = 1; pl.ngroups = 0; pl.rpc = 0;
-        pl.smem = cta_smem;
-        pl.group_bytes = 0;
+        if (!one_fits) return ELA_ERR_UNSUPPORTED;
+        pl.S = 1; pl.ngroups = 0; pl.rpc = (int)N;
+        pl.smem = one_smem;
+        pl.seg_bytes = 0;
         pl.ws_bytes = ELA_WS_HEADER;
     } else if (chosen == ELA_PATH_GRID) {
-        if (!grid_fits) return ELA_ERR_UNSUPPORTED;
+        if (!multi_fits) return ELA_ERR_UNSUPPORTED;
         pl.S = S; pl.ngroups = ngroups; pl.rpc = rpc;
-        pl.smem = grid_smem_b;
-        pl.group_bytes = group_layout<R>(N, M).total;
-        pl.ws_bytes = ELA_WS_HEADER + (size_t)ngroups * pl.group_bytes;
+        pl.smem = multi_smem;
+        pl.seg_bytes = align_up(8 + 8 * (size_t)Ex<R>::EW * rpc, 128);
+        pl.ws_bytes = ELA_WS_HEADER + (size_t)ngroups * 2 * S * pl.seg_bytes;
     } else {
         return ELA_ERR_ARGUMENT;
     }
@@ -838,7 +799,7 @@ int device_limits(int& sms, size_t& smem_max) {
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return ELA_ERR_CUDA;
     sms = v;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return ELA_ERR_CUDA;
-    smem_max = (size_t)v - 1024;  // room for the kernels' static shared variables
+    smem_max = (size_t)v - 3 * 1024;  // room for the kernel's static shared variables
     return ELA_OK;
 }
 
@@ -857,28 +818,83 @@ int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl) {
 
 template <typename In, typename R>
 int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
-    if (pl.path == ELA_PATH_CTA) {
-        auto kern = auction_cta_kernel<In, R>;
+    if (pl.S == 1) {
+        auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, ELA_UNROLL_ONE>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
         const int64_t grid = p.B < (1ll << 20) ? p.B : (1ll << 20);
-        kern<<<(unsigned int)grid, ELA_CTA_THREADS, pl.smem, stream>>>(p);
+        kern<<<(unsigned int)grid, ELA_THREADS_ONE, pl.smem, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
-    auto kern = auction_grid_kernel<In, R>;
+    auto kern = auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI, ELA_UNROLL_MULTI>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
         return ELA_ERR_CUDA;
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, ELA_GRID_THREADS, pl.smem) != cudaSuccess)
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, ELA_THREADS_MULTI, pl.smem) != cudaSuccess)
         return ELA_ERR_CUDA;
     if (occ < 1) return ELA_ERR_UNSUPPORTED;
-    // Every CTA of a group waits on the others, so all of them must be resident:
-    // the cooperative launch refuses a grid that cannot be co-scheduled.
+    // The CTAs of a group wait on one another, so all must be resident at
+    // once: the cooperative launch refuses a grid that cannot be co-scheduled.
     Params pc = p;
     void* args[] = {&pc};
     const cudaError_t e = cudaLaunchCooperativeKernel((const void*)kern, dim3(pl.S * pl.ngroups),
-                                                      dim3(ELA_GRID_THREADS), args, pl.smem, stream);
+                                                      dim3(ELA_THREADS_MULTI), args, pl.smem, stream);
     return e == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
+}
+
+// Validates the arguments common to the solve entry points and fills Params
+// (everything except the workspace pointers).
+int fill_params(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, int64_t stride_b,
+                int64_t stride_n, const double* eps_schedule, int n_eps, int max_iter,
+                int64_t* assign_out, void* prices_out, int64_t* stats_out, Params& p) {
+    const int es = elem_size(dtype);
+    if (!cost || !assign_out || !prices_out) return ELA_ERR_ARGUMENT;
+    if (stride_n < M || (B > 1 && stride_b < (N - 1) * stride_n + M)) return ELA_ERR_ARGUMENT;
+    memset(&p, 0, sizeof(p));
+    p.cost = cost;
+    p.B = B; p.N = N; p.M = M; p.stride_b = stride_b; p.stride_n = stride_n;
+    for (int k = 0; k < n_eps; ++k) p.eps[k] = eps_schedule[k];
+    p.n_eps = n_eps;
+    p.max_iter = max_iter;
+    p.vec_ok = ((reinterpret_cast<uintptr_t>(cost) & 15u) == 0) && ((stride_n * es) % 16 == 0) &&
+               ((stride_b * es) % 16 == 0) && ((M * es) % 16 == 0);
+    p.assign_out = assign_out;
+    p.prices_out = prices_out;
+    p.stats_out = stats_out;
+    p.wait_ns = g_wait_ns;
+    p.skip_publish = g_skip_publish;
+    return ELA_OK;
+}
+
+// Argument checks that need no device; returns ELA_OK to continue, or a
+// status.  *done is set when there is nothing to solve (after clearing outputs).
+int check_common(int dtype, int64_t B, int64_t N, int64_t M, const double* eps_schedule, int n_eps,
+                 int max_iter, void* prices_out, int64_t* stats_out, int32_t* status_out,
+                 cudaStream_t s, bool* done) {
+    *done = false;
+    if (elem_size(dtype) == 0 || B < 0 || N < 0 || M < 0 || max_iter < 0) return ELA_ERR_ARGUMENT;
+    if (n_eps < 1 || n_eps > ELA_MAX_PHASES || eps_schedule == nullptr) return ELA_ERR_ARGUMENT;
+    for (int k = 0; k < n_eps; ++k)
+        if (!(eps_schedule[k] > 0.0) || eps_schedule[k] == INFINITY) return ELA_ERR_ARGUMENT;
+    if (B == 0 || N == 0) {
+        *done = true;
+        if (B > 0 && M > 0 && prices_out &&
+            cudaMemsetAsync(prices_out, 0, (size_t)(B * M) * (dtype == ELA_DTYPE_F64 ? 8 : 4), s) != cudaSuccess)
+            return ELA_ERR_CUDA;
+        if (stats_out && B > 0 && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess)
+            return ELA_ERR_CUDA;
+        if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
+    }
+    return ELA_OK;
+}
+
+int dispatch(int dtype, const Params& p, const Plan& pl, cudaStream_t s) {
+    switch (dtype) {
+    case ELA_DTYPE_F32: return launch<float, float>(p, pl, s);
+    case ELA_DTYPE_F16: return launch<__half, float>(p, pl, s);
+    case ELA_DTYPE_BF16: return launch<__nv_bfloat16, float>(p, pl, s);
+    default: return launch<double, double>(p, pl, s);
+    }
 }
 
 }  // namespace
@@ -907,68 +923,37 @@ size_t ela_auction_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t M, i
 
 void ela_auction_set_wait_limit_ns(uint64_t ns) { g_wait_ns = ns ? ns : 1; }
 
-void ela_auction_debug_skip_arrive(int on) { g_skip_arrive = on ? 1 : 0; }
+void ela_auction_debug_skip_arrive(int on) { g_skip_publish = on ? 1 : 0; }
 
 int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
                       int64_t stride_b, int64_t stride_n, const double* eps_schedule,
                       int n_eps, int max_iter, int path, int64_t* assign_out,
                       void* prices_out, int64_t* stats_out, int32_t* status_out,
                       void* workspace, size_t workspace_bytes, void* stream) {
-    const int es = elem_size(dtype);
-    if (es == 0 || B < 0 || N < 0 || M < 0 || max_iter < 0) return ELA_ERR_ARGUMENT;
-    if (n_eps < 1 || n_eps > ELA_MAX_PHASES || eps_schedule == nullptr) return ELA_ERR_ARGUMENT;
-    for (int k = 0; k < n_eps; ++k)
-        if (!(eps_schedule[k] > 0.0) || eps_schedule[k] == INFINITY) return ELA_ERR_ARGUMENT;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    if (B == 0 || N == 0) {
-        if (B > 0 && M > 0 && prices_out &&
-            cudaMemsetAsync(prices_out, 0, (size_t)(B * M) * (dtype == ELA_DTYPE_F64 ? 8 : 4), s) != cudaSuccess)
-            return ELA_ERR_CUDA;
-        if (stats_out && B > 0 && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess)
-            return ELA_ERR_CUDA;
-        if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
-        return ELA_OK;
-    }
-    if (!cost || !assign_out || !prices_out || !workspace) return ELA_ERR_ARGUMENT;
-    if (stride_n < M || (B > 1 && stride_b < (N - 1) * stride_n + M)) return ELA_ERR_ARGUMENT;
-    if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return ELA_ERR_ARGUMENT;
+    bool done = false;
+    int rc = check_common(dtype, B, N, M, eps_schedule, n_eps, max_iter, prices_out, stats_out, status_out, s, &done);
+    if (rc != ELA_OK || done) return rc;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return ELA_ERR_ARGUMENT;
+    Params p;
+    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, assign_out,
+                     prices_out, stats_out, p);
+    if (rc != ELA_OK) return rc;
     Plan pl;
-    int rc = make_plan(dtype, B, N, M, path, pl);
+    rc = make_plan(dtype, B, N, M, path, pl);
     if (rc != ELA_OK) return rc;
     if (workspace_bytes < pl.ws_bytes) return ELA_ERR_ARGUMENT;
-
-    Params p;
-    memset(&p, 0, sizeof(p));
-    p.cost = cost;
-    p.B = B; p.N = N; p.M = M; p.stride_b = stride_b; p.stride_n = stride_n;
-    for (int k = 0; k < n_eps; ++k) p.eps[k] = eps_schedule[k];
-    p.n_eps = n_eps;
-    p.max_iter = max_iter;
-    p.vec_ok = ((reinterpret_cast<uintptr_t>(cost) & 15u) == 0) && ((stride_n * es) % 16 == 0) &&
-               ((stride_b * es) % 16 == 0) && ((M * es) % 16 == 0);
-    p.assign_out = assign_out;
-    p.prices_out = prices_out;
-    p.stats_out = stats_out;
     unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
     p.status = status_out ? status_out : reinterpret_cast<int32_t*>(ws + 4);
     p.ws = ws;
-    p.group_bytes = pl.group_bytes;
+    p.seg_bytes = pl.seg_bytes;
     p.S = pl.S;
     p.ngroups = pl.ngroups;
     p.rows_per_cta = pl.rpc;
-    p.wait_ns = g_wait_ns;
-    p.skip_arrive = g_skip_arrive;
-
     if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
-
-    switch (dtype) {
-    case ELA_DTYPE_F32: return launch<float, float>(p, pl, s);
-    case ELA_DTYPE_F16: return launch<__half, float>(p, pl, s);
-    case ELA_DTYPE_BF16: return launch<__nv_bfloat16, float>(p, pl, s);
-    default: return launch<double, double>(p, pl, s);
-    }
+    return dispatch(dtype, p, pl, s);
 }
 
 }  // extern "C"

@@ -87,8 +87,8 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
- * Limit, in nanoseconds, on every device-side wait of the grid path (the
- * per-round barrier between the CTAs that share one problem).  A wait that
+ * Limit, in nanoseconds, on every device-side wait of the grid path (each
+ * round's exchange of bids between the CTAs that share one problem).  A wait that
  * runs out writes ELA_ERR_TIMEOUT to *status_out and the kernel returns.
  * Default 2 s.  Process-wide setting.
  */
@@ -96,8 +96,8 @@ void ela_auction_set_wait_limit_ns(uint64_t ns);
 
 /*
  * Test hook for the timeout path.  When `on` is nonzero, CTA 0 of every group
- * of the grid path leaves out its arrival at the first round barrier, so the
- * other CTAs' bounded wait runs out and the solve ends with ELA_ERR_TIMEOUT
+ * of the grid path never publishes its first round's bids, so every CTA's
+ * bounded wait for them runs out and the solve ends with ELA_ERR_TIMEOUT
  * (no fault, no hang; the CUDA context stays usable).  Process-wide setting.
  */
 void ela_auction_debug_skip_arrive(int on);
