@@ -27,6 +27,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "ela_auction.h"
@@ -897,6 +898,31 @@ int dispatch(int dtype, const Params& p, const Plan& pl, cudaStream_t s) {
     }
 }
 
+// ------------------------------------------------- allocation-free variant
+// Scratch for ela_auction_solve_noalloc: a fixed array in every device's global
+// memory, reserved when the library is loaded and held until the process
+// exits.  Host code sees only a stand-in symbol; the device address comes from
+// cudaGetSymbolAddress, looked up once per device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[ELA_NOALLOC_SCRATCH_BYTES];
+
+#define ELA_MAX_DEVICES 64
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[ELA_MAX_DEVICES] = {nullptr};
+
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ELA_ERR_CUDA;
+    if (dev < 0 || dev >= ELA_MAX_DEVICES) return ELA_ERR_UNSUPPORTED;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* ptr = nullptr;
+        if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return ELA_ERR_CUDA;
+        g_noalloc_ptr[dev] = ptr;
+    }
+    *out = g_noalloc_ptr[dev];
+    return ELA_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -951,6 +977,43 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
     p.ngroups = pl.ngroups;
     p.rows_per_cta = pl.rpc;
     if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
+    return dispatch(dtype, p, pl, s);
+}
+
+
+// Same solve as ela_auction_solve, with its scratch in g_noalloc_scratch
+// instead of a caller-supplied workspace; see include/ela_auction.h.
+int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
+                              int64_t stride_b, int64_t stride_n, const double* eps_schedule,
+                              int n_eps, int max_iter, int path, int64_t* assign_out,
+                              void* prices_out, int64_t* stats_out, int32_t* status_out, void* stream) {
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    bool done = false;
+    int rc = check_common(dtype, B, N, M, eps_schedule, n_eps, max_iter, prices_out, stats_out, status_out, s, &done);
+    if (rc != ELA_OK || done) return rc;
+    Params p;
+    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, assign_out,
+                     prices_out, stats_out, p);
+    if (rc != ELA_OK) return rc;
+    Plan pl;
+    rc = make_plan(dtype, B, N, M, path, pl);
+    if (rc != ELA_OK) return rc;
+    if (pl.ws_bytes > (size_t)ELA_NOALLOC_SCRATCH_BYTES) return ELA_ERR_UNSUPPORTED;
+    void* scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc != ELA_OK) return rc;
+    unsigned char* ws = reinterpret_cast<unsigned char*>(scratch);
+    p.status = status_out ? status_out : reinterpret_cast<int32_t*>(ws + 4);
+    p.ws = ws;
+    p.seg_bytes = pl.seg_bytes;
+    p.S = pl.S;
+    p.ngroups = pl.ngroups;
+    p.rows_per_cta = pl.rpc;
+    // The array keeps the previous call's contents: clear the part this solve
+    // uses (abort flag, status word, exchange tags must start at zero).
+    if (cudaMemsetAsync(scratch, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
     return dispatch(dtype, p, pl, s);

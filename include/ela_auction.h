@@ -102,6 +102,40 @@ void ela_auction_set_wait_limit_ns(uint64_t ns);
  */
 void ela_auction_debug_skip_arrive(int on);
 
+/*
+ * Size of the fixed device scratch array behind ela_auction_solve_noalloc:
+ * 4 MiB, held in every GPU's memory from library load until process exit.
+ */
+#define ELA_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+/*
+ * ela_auction_solve without a workspace argument, for callers that cannot
+ * allocate device memory themselves: hosts that own the GPU through a
+ * pre-reserved memory pool in which a cudaMalloc would fail or fragment, code
+ * that must not trigger cudaMalloc's implicit device synchronisation, and
+ * foreign-language bindings with no access to a device allocator.  It has no
+ * counterpart in the reference, which allocates its scratch inside the call.
+ *
+ * Arguments, results and status codes are those of ela_auction_solve; the
+ * caller still provides cost, assignment, price, stats and status buffers.
+ * The solve's scratch lives in a library-owned static device array of
+ * ELA_NOALLOC_SCRATCH_BYTES bytes; sizes whose scratch would not fit return
+ * ELA_ERR_UNSUPPORTED before any work is enqueued.  The call allocates
+ * nothing (no cudaMalloc, no cudaFree, no allocating library routine).
+ *
+ * The first call on a device looks up that device's address of the array
+ * (cudaGetSymbolAddress, with the device current); make that first call
+ * before any stream capture.  All calls on a device share the one array and
+ * each call clears the part it uses, so calls whose work overlaps on the GPU
+ * (different streams, or concurrent host threads) race and give wrong
+ * results: order them, e.g. on one stream.
+ */
+int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
+                              int64_t stride_b, int64_t stride_n, const double* eps_schedule,
+                              int n_eps, int max_iter, int path, int64_t* assign_out,
+                              void* prices_out, int64_t* stats_out, int32_t* status_out,
+                              void* stream);
+
 #ifdef __cplusplus
 }
 #endif
