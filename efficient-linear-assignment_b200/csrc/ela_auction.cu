@@ -35,6 +35,18 @@
 #define ELA_MAX_PHASES 32
 #define ELA_SMALL_M 128           // below this torch.topk uses introselect
 
+#ifdef ELA_PROF
+__device__ unsigned long long g_prof[16];
+__device__ unsigned long long g_trace[8192][8];
+#define PROF_MARK(var) long long var = clock64()
+#define PROF_ADDALL(slot, v) do { if (threadIdx.x == 0) atomicAdd(&g_prof[slot], (unsigned long long)(v)); } while (0)
+#define PROF_ADD(slot, a, b) do { if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&g_prof[slot], (unsigned long long)((b) - (a))); } while (0)
+#else
+#define PROF_MARK(var)
+#define PROF_ADD(slot, a, b)
+#define PROF_ADDALL(slot, v)
+#endif
+
 namespace {
 
 // ---------------------------------------------------------------- arithmetic
@@ -118,6 +130,12 @@ template <> struct Elem<double> {
 // written during a solve.
 __device__ __forceinline__ uint4 ld_stream16(const void* ptr) {
     uint4 r;
+#ifdef ELA_LD_CG
+    asm("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+        : "l"(ptr));
+    return r;
+#endif
     asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
         : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
         : "l"(ptr));
@@ -137,15 +155,20 @@ template <typename R> __device__ __forceinline__ void top2_init(Top2<R>& t) {
     t.v1 = -INFINITY; t.v2 = -INFINITY; t.p1 = -1; t.p2 = -1;
 }
 
+template <typename R> __device__ __forceinline__ R rmax(R a, R b) { return a > b ? a : b; }
+template <typename R> __device__ __forceinline__ R rmin(R a, R b) { return a < b ? a : b; }
+template <> __device__ __forceinline__ float rmax<float>(float a, float b) { return fmaxf(a, b); }
+template <> __device__ __forceinline__ float rmin<float>(float a, float b) { return fminf(a, b); }
+
 template <typename R> __device__ __forceinline__ void top2_add(Top2<R>& t, R v, int col) {
-    if (t.p1 < 0 || v > t.v1) {
-        t.v2 = t.v1; t.v1 = v; t.p1 = col; t.p2 = -1;
-    } else if (v == t.v1) {
-        if (t.p2 < 0) t.p2 = col;
-        t.v2 = v;
-    } else if (v > t.v2) {
-        t.v2 = v;
-    }
+    // branch-free (selects and min/max only), so the lanes of a warp never
+    // diverge here; values are never NaN (finite costs and prices)
+    const bool gt = (v > t.v1) || (t.p1 < 0);
+    const bool eq = (v == t.v1);
+    t.v2 = gt ? t.v1 : rmax(t.v2, v);
+    t.p2 = gt ? -1 : ((eq && t.p2 < 0) ? col : t.p2);
+    t.v1 = gt ? v : t.v1;
+    t.p1 = gt ? col : t.p1;
 }
 
 // Merge two disjoint column sets; commutative, so a butterfly leaves every
@@ -181,6 +204,39 @@ template <typename R> __device__ __forceinline__ Top2<R> top2_warp(Top2<R> t) {
         t = top2_merge(t, o);
     }
     return t;
+}
+
+// fp32: the same reduction with warp-wide integer reductions (redux.sync) on
+// order-preserving keys of the values.  -0 and +0 compare equal in the
+// reference's comparisons, so both map to the key of +0.
+__device__ __forceinline__ unsigned int fkey(float v) {
+    unsigned int u = __float_as_uint(v + 0.0f);  // -0 + +0 = +0
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float fkey_inv(unsigned int k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+template <> __device__ __forceinline__ Top2<float> top2_warp<float>(Top2<float> t) {
+    const int big = 0x7fffffff;
+    const bool live = t.p1 >= 0;
+    const unsigned int k1 = live ? fkey(t.v1) : 0u;
+    const unsigned int K1 = __reduce_max_sync(0xffffffffu, k1);
+    const bool top = live && k1 == K1;
+    const unsigned int ntop = __popc(__ballot_sync(0xffffffffu, top));
+    // second value: the maximum wins twice, else the best of the rest
+    const unsigned int k2 = !live ? 0u : (top ? (t.v2 == -INFINITY ? 0u : fkey(t.v2)) : k1);
+    const unsigned int K2 = __reduce_max_sync(0xffffffffu, k2);
+    // first two columns holding the maximum (columns are distinct across lanes)
+    const int P1 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)(top ? t.p1 : big));
+    const int own2 = (t.p2 >= 0) ? t.p2 : big;
+    const int cand = top ? ((t.p1 == P1) ? own2 : t.p1) : big;
+    const int P2 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)cand);
+    Top2<float> r;
+    r.p1 = (K1 == 0u) ? -1 : P1;
+    r.v1 = (K1 == 0u) ? -INFINITY : fkey_inv(K1);
+    r.p2 = (P2 == big) ? -1 : P2;
+    r.v2 = (ntop >= 2 || r.p2 >= 0) ? r.v1 : (K2 == 0u ? -INFINITY : fkey_inv(K2));
+    return r;
 }
 
 // ------------------------------------------------- small-row tie resolution
@@ -312,9 +368,58 @@ struct Params {
 };
 
 // ------------------------------------------------------------ row scanning
+// W consecutive prices from shared memory (one or two vector loads).
+template <typename R, int W> __device__ __forceinline__ void load_prices(const R* Ps, int c0, R* out) {
+    if (sizeof(R) * W == 16) {
+        const float4 q = *reinterpret_cast<const float4*>(Ps + c0);
+        const R* r = reinterpret_cast<const R*>(&q);
+#pragma unroll
+        for (int e = 0; e < W; ++e) out[e] = r[e];
+    } else if (sizeof(R) * W == 32) {
+        const float4 q0 = *reinterpret_cast<const float4*>(Ps + c0);
+        const float4 q1 = *(reinterpret_cast<const float4*>(Ps + c0) + 1);
+        const R* r0 = reinterpret_cast<const R*>(&q0);
+        const R* r1 = reinterpret_cast<const R*>(&q1);
+#pragma unroll
+        for (int e = 0; e < W / 2; ++e) { out[e] = r0[e]; out[W / 2 + e] = r1[e]; }
+    } else {
+#pragma unroll
+        for (int e = 0; e < W; ++e) out[e] = Ps[c0 + e];
+    }
+}
+
+// Lane-local top-2 over chunks base, base+stride, ... (UNROLL chunks per
+// batch).  Chunks are 16-byte vectors of W elements.
+template <typename In, typename R, int UNROLL>
+__device__ __forceinline__ void scan_chunks(const uint4* rv, const R* __restrict__ Ps, int base, int stride,
+                                            int nchunks, Top2<R>& t) {
+    constexpr int W = Elem<In>::W;
+    for (; base < nchunks; base += stride * UNROLL) {
+        uint4 raw[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int ch = base + u * stride;
+            if (ch < nchunks) raw[u] = ld_stream16(rv + ch);
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int ch = base + u * stride;
+            if (ch < nchunks) {
+                R x[W], pr[W];
+                Elem<In>::template unpack<R>(raw[u], x);
+                load_prices<R, W>(Ps, ch * W, pr);
+#pragma unroll
+                for (int e = 0; e < W; ++e) top2_add(t, sub_rn(-x[e], pr[e]), ch * W + e);
+            }
+        }
+    }
+}
+
 // Top-2 over the columns of one row that this warp covers: the row's 16-byte
 // chunks are dealt to `wpr` warps in turn (warp `sub` takes chunks
-// sub*32+lane, sub*32+lane+32*wpr, ...).  The result is reduced over the warp.
+// sub*32+lane, sub*32+lane+32*wpr, ...).  The batch size follows the number
+// of chunks per lane, so no predicated-off batch slots are issued.  The
+// result is reduced over the warp.
 template <typename In, typename R, int UNROLL>
 __device__ __forceinline__ Top2<R> scan_row(const Params& p, const In* row, const R* __restrict__ Ps,
                                             int lane, int sub, int wpr) {
@@ -325,25 +430,13 @@ __device__ __forceinline__ Top2<R> scan_row(const Params& p, const In* row, cons
         constexpr int W = Elem<In>::W;
         const int nchunks = M / W;
         const int stride = 32 * wpr;
+        const int per_lane = (nchunks + stride - 1) / stride;
         const uint4* rv = reinterpret_cast<const uint4*>(row);
-        for (int base = sub * 32 + lane; base < nchunks; base += stride * UNROLL) {
-            uint4 raw[UNROLL];
-#pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
-                const int ch = base + u * stride;
-                if (ch < nchunks) raw[u] = ld_stream16(rv + ch);
-            }
-#pragma unroll
-            for (int u = 0; u < UNROLL; ++u) {
-                const int ch = base + u * stride;
-                if (ch < nchunks) {
-                    R x[W];
-                    Elem<In>::template unpack<R>(raw[u], x);
-#pragma unroll
-                    for (int e = 0; e < W; ++e) top2_add(t, sub_rn(-x[e], Ps[ch * W + e]), ch * W + e);
-                }
-            }
-        }
+        const int base = sub * 32 + lane;
+        if (per_lane <= 1) scan_chunks<In, R, 1>(rv, Ps, base, stride, nchunks, t);
+        else if (per_lane <= 2) scan_chunks<In, R, 2>(rv, Ps, base, stride, nchunks, t);
+        else if (per_lane <= 4 || UNROLL <= 4) scan_chunks<In, R, 4>(rv, Ps, base, stride, nchunks, t);
+        else scan_chunks<In, R, UNROLL>(rv, Ps, base, stride, nchunks, t);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
             top2_add(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), col);
@@ -468,7 +561,9 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 #define ELA_UNROLL_ONE 4
 #define ELA_THREADS_MULTI 512
 #define ELA_MINB_MULTI 1
+#ifndef ELA_UNROLL_MULTI
 #define ELA_UNROLL_MULTI 8
+#endif
 #define ELA_MAX_S 256
 #define ELA_WS_HEADER 256
 
@@ -531,6 +626,7 @@ auction_kernel(const Params p) {
             }
             const R eps = (R)p.eps[ph];
             const unsigned int t1 = t + 1;
+            PROF_MARK(pt0);
             // ---- own rows that bid this round
             if (tid == 0) { s_nact = 0; s_total = 0; s_extra = 0; s_fail = 0; }
             __syncthreads();
@@ -538,6 +634,7 @@ auction_kernel(const Params p) {
                 if (rowcol[q] < 0) active[atomicAdd(&s_nact, 1)] = q;
             __syncthreads();
             const int K = s_nact;
+            PROF_MARK(pt1);
             unsigned long long* myseg =
                 reinterpret_cast<unsigned long long*>(gbase + (size_t)((t & 1) * S + c) * p.seg_bytes);
             // ---- bids against the round-start prices.  With few rows, a row is
@@ -557,12 +654,25 @@ auction_kernel(const Params p) {
                     const In* row = base + (int64_t)i * p.stride_n;
                     Top2<R> tt;
                     top2_init(tt);
+#ifdef ELA_SCAN_TWICE
+                    if (has) { long long q0 = clock64(); tt = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                               if (lane == 0 && t < 8192) atomicMax(&g_trace[t][4], (unsigned long long)(clock64() - q0)); }
+#endif
+                    PROF_MARK(ps0);
                     if (has) tt = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+#ifdef ELA_PROF
+                    { long long ps1 = clock64();
+                      if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][7], (unsigned long long)(ps1 - ps0)); }
+#endif
                     if (wpr > 1) {
                         if (has && lane == 0) wtop[warp] = tt;
                         __syncthreads();
-                        if (has && sub == 0)
-                            for (int w = 1; w < wpr; ++w) tt = top2_merge(tt, wtop[warp + w]);
+                        if (has && sub == 0) {  // lanes fetch the group's partial results; butterfly merge
+                            Top2<R> o;
+                            top2_init(o);
+                            if (lane < wpr) o = wtop[warp + lane];
+                            tt = top2_warp(o);
+                        }
                     }
                     if (has && sub == 0) {
                         int j1;
@@ -578,6 +688,7 @@ auction_kernel(const Params p) {
                 }
             }
             __syncthreads();
+            PROF_MARK(pt2);
             // ---- gather the round's bids of the whole problem
             int ntot;
             if (!MULTI) {
@@ -595,6 +706,9 @@ auction_kernel(const Params p) {
                     for (;;) {  // bounded wait for the segment's header
                         const unsigned long long h = ld_relaxed_u64(seg);
                         if ((unsigned int)(h >> 32) == t1) { cntv = (int)(unsigned int)(h & 0xffffffffull); break; }
+#ifdef ELA_POLL_SLEEP
+                        __nanosleep(ELA_POLL_SLEEP);
+#endif
                         if ((++spins & 15u) == 0) {
                             if (*(volatile int*)abort_flag) break;
                             if (globaltimer_ns() - t0 > p.wait_ns) {
@@ -629,6 +743,8 @@ auction_kernel(const Params p) {
                     }
                 }
                 __syncthreads();
+                PROF_MARK(pt2b);
+                PROF_ADDALL(8, pt2b - pt2);
                 if (s_fail) return;
                 if (s_extra) {  // rounds with many bids: read the remaining entries together
                     for (int sg = 0; sg < S; ++sg) {
@@ -657,6 +773,7 @@ auction_kernel(const Params p) {
                 ntot = s_total;
             }
             ++t;
+            PROF_MARK(pt3);
             if (ntot == 0) {  // nobody bid: this epsilon's solve has converged
                 if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
@@ -689,6 +806,25 @@ auction_kernel(const Params p) {
             for (int e = tid; e < ntot; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
             ++it;
             __syncthreads();
+            PROF_MARK(pt4);
+            PROF_ADD(0, pt0, pt1); PROF_ADD(1, pt1, pt2); PROF_ADD(2, pt2, pt3); PROF_ADD(3, pt3, pt4);
+            PROF_ADD(4, 0, 1); PROF_ADD(5, 0, (K > 0));
+            if (K > 0) { PROF_ADDALL(6, pt2 - pt1); PROF_ADDALL(7, 1); PROF_ADDALL(10, K); }
+            PROF_ADDALL(9, 1);
+            PROF_ADDALL(11, pt3 - pt2);
+#ifdef ELA_PROF
+            if (t - 1 < 8192) {
+                if (threadIdx.x == 0 && K > 0) atomicMax(&g_trace[t - 1][5], (unsigned long long)(pt2 - pt1));
+                if (threadIdx.x == 0 && K > 0) atomicMax(&g_trace[t - 1][6], (unsigned long long)K);
+                if (blockIdx.x == 0 && threadIdx.x == 0) {
+                    g_trace[t - 1][0] = ntot; g_trace[t - 1][1] = pt1 - pt0; g_trace[t - 1][2] = pt2 - pt1;
+                    g_trace[t - 1][3] = pt3 - pt2;
+#ifndef ELA_SCAN_TWICE
+                    g_trace[t - 1][4] = pt4 - pt3;
+#endif
+                }
+            }
+#endif
         }
         // ---- outputs of problem b
         if (tid == 0) s_unassigned = 0;
@@ -1019,4 +1155,9 @@ int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N,
     return dispatch(dtype, p, pl, s);
 }
 
+#ifdef ELA_PROF
+void ela_prof_read(unsigned long long* out) { cudaMemcpyFromSymbol(out, g_prof, sizeof(g_prof)); }
+void ela_trace_read(unsigned long long* out) { cudaMemcpyFromSymbol(out, g_trace, sizeof(g_trace)); }
+void ela_prof_reset(void) { unsigned long long z[16] = {0}; cudaMemcpyToSymbol(g_prof, z, sizeof(z)); }
+#endif
 }  // extern "C"
