@@ -43,6 +43,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--fixed-eps", action="store_true",
+                    help="reference mode: constant epsilon 1e-2 instead of the cfg2 epsilon schedule")
     return ap.parse_args()
 
 
@@ -176,7 +179,7 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    sched = ela.workloads.CFG2_SCHEDULE
+    sched = [1e-2] if args.fixed_eps else ela.workloads.CFG2_SCHEDULE
     cost_cpu = ela.workloads.cfg2()
     cost = cost_cpu.to(dev)
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)  # > 126 MB L2
@@ -218,7 +221,7 @@ def main():
     host_cost = cost_cpu.pin_memory()
     host_idx = torch.empty((1, N_MAIN), dtype=torch.int64).pin_memory()
     e2e_ms = []
-    for k in range(args.warmup + args.steps):
+    for k in range(0 if args.no_e2e else args.warmup + args.steps):
         flush.zero_()
         torch.cuda.synchronize()
         e0 = torch.cuda.Event(enable_timing=True)
@@ -231,7 +234,7 @@ def main():
         torch.cuda.synchronize()
         if k >= args.warmup:
             e2e_ms.append(e0.elapsed_time(e1))
-    e2e_val = max_over_ranks(statistics.mean(e2e_ms)) / world
+    e2e_val = max_over_ranks(statistics.mean(e2e_ms)) / world if e2e_ms else None
 
     # batched config 4, sharded over the ranks
     batched = None
@@ -273,7 +276,8 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded uniform[0,1), seed 1; cfg4 seed 3)",
-            "config": {"workload": "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps",
+            "config": {"workload": ("cfg2 (fixed eps 1e-2): B=1 N=M=4096 fp32, max_iter 1000" if args.fixed_eps else
+                                    "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps"),
                        "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) between steps",
                        "rounds": rounds, "row_bids": row_bids},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -281,7 +285,7 @@ def main():
                          "peak_kind": peak_kind,
                          "alg_bytes_per_launch": alg_bytes},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e_val, 4), "unit": "ms/solve",
+            "e2e": None if e2e_val is None else {"value": round(e2e_val, 4), "unit": "ms/solve",
                     "h2d_bytes_per_step": cost_cpu.numel() * 4, "d2h_bytes_per_step": N_MAIN * 8},
             "gpu_launches": args.steps,
             "batched": batched,
