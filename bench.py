@@ -240,8 +240,10 @@ def main():
     batched = None
     if not args.no_batched:
         B4 = 256
-        per = B4 // world
-        c4 = ela.workloads.cfg4()[rank * per:(rank + 1) * per].contiguous().to(dev)
+        from efficient_linear_assignment_b200.sharding import shard_range
+        lo, hi = shard_range(B4, world, rank)
+        per = hi - lo
+        c4 = ela.workloads.cfg4()[lo:hi].contiguous().to(dev)
         for _ in range(args.warmup):
             r4 = ela.auction_solve_op(c4, [1e-2], 1000, ela.PATH_AUTO)
         torch.cuda.synchronize()

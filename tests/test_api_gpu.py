@@ -124,3 +124,12 @@ def test_wait_timeout_reports_status_and_context_survives():
     a, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_GRID)
     b, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_CTA)
     assert torch.equal(a, b)
+
+
+def test_multi_device_sharding_matches_single_solve():
+    from efficient_linear_assignment_b200.sharding import solve_multi_device
+    cost = ela.workloads.cfg4(B=12, N=128).to(dev)
+    ref_a, ref_p, _ = ela.solve(cost, 1e-2)
+    devs = [torch.device("cuda", i) for i in range(torch.cuda.device_count())]
+    a, p = solve_multi_device(cost, devs, lambda c: ela.solve(c, 1e-2)[:2])
+    assert torch.equal(a, ref_a) and torch.equal(p, ref_p)
