@@ -37,7 +37,7 @@
 
 #ifdef ELA_PROF
 __device__ unsigned long long g_prof[16];
-__device__ unsigned long long g_trace[8192][8];
+__device__ unsigned long long g_trace[8192][12];
 #define PROF_MARK(var) long long var = clock64()
 #define PROF_ADDALL(slot, v) do { if (threadIdx.x == 0) atomicAdd(&g_prof[slot], (unsigned long long)(v)); } while (0)
 #define PROF_ADD(slot, a, b) do { if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&g_prof[slot], (unsigned long long)((b) - (a))); } while (0)
@@ -130,15 +130,26 @@ template <> struct Elem<double> {
 // written during a solve.
 __device__ __forceinline__ uint4 ld_stream16(const void* ptr) {
     uint4 r;
-#ifdef ELA_LD_CG
-    asm("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-        : "l"(ptr));
-    return r;
-#endif
+#if defined(ELA_LD_CG)
+    asm("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
+#elif defined(ELA_LD_NC_L1)
+    asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
+#elif defined(ELA_LD_CA)
+    asm("ld.global.ca.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
+#elif defined(ELA_LD_EVL)
+    unsigned long long pol;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr), "l"(pol));
+#elif defined(ELA_LD_NC_L1_EVL)
+    unsigned long long pol;
+    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+    asm("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr), "l"(pol));
+#else
     asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-        : "l"(ptr));
+        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
+#endif
     return r;
 }
 
@@ -222,20 +233,23 @@ template <> __device__ __forceinline__ Top2<float> top2_warp<float>(Top2<float> 
     const unsigned int k1 = live ? fkey(t.v1) : 0u;
     const unsigned int K1 = __reduce_max_sync(0xffffffffu, k1);
     const bool top = live && k1 == K1;
-    const unsigned int ntop = __popc(__ballot_sync(0xffffffffu, top));
-    // second value: the maximum wins twice, else the best of the rest
+    // independent of one another once K1 is known:
+    const int P1 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)(top ? t.p1 : big));
     const unsigned int k2 = !live ? 0u : (top ? (t.v2 == -INFINITY ? 0u : fkey(t.v2)) : k1);
     const unsigned int K2 = __reduce_max_sync(0xffffffffu, k2);
-    // first two columns holding the maximum (columns are distinct across lanes)
-    const int P1 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)(top ? t.p1 : big));
-    const int own2 = (t.p2 >= 0) ? t.p2 : big;
-    const int cand = top ? ((t.p1 == P1) ? own2 : t.p1) : big;
-    const int P2 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)cand);
+    const unsigned int topmask = __ballot_sync(0xffffffffu, top);
+    const bool tie = (__popc(topmask) >= 2) || __any_sync(0xffffffffu, top && t.p2 >= 0);
     Top2<float> r;
     r.p1 = (K1 == 0u) ? -1 : P1;
     r.v1 = (K1 == 0u) ? -INFINITY : fkey_inv(K1);
-    r.p2 = (P2 == big) ? -1 : P2;
-    r.v2 = (ntop >= 2 || r.p2 >= 0) ? r.v1 : (K2 == 0u ? -INFINITY : fkey_inv(K2));
+    r.p2 = -1;
+    r.v2 = (K2 == 0u) ? -INFINITY : fkey_inv(K2);
+    if (tie) {  // rare: the maximum occurs twice; find its second column
+        const int own2 = (t.p2 >= 0) ? t.p2 : big;
+        const int cand = top ? ((t.p1 == P1) ? own2 : t.p1) : big;
+        r.p2 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)cand);
+        r.v2 = r.v1;
+    }
     return r;
 }
 
@@ -365,6 +379,7 @@ struct Params {
     int rows_per_cta;        // ceil(N / S)
     unsigned long long wait_ns;
     int skip_publish;        // test hook: CTA 0 never publishes its first round
+    int max_wpr;             // most warps that share one row's scan (power of two)
 };
 
 // ------------------------------------------------------------ row scanning
@@ -415,14 +430,140 @@ __device__ __forceinline__ void scan_chunks(const uint4* rv, const R* __restrict
     }
 }
 
+// ---- fast scan: (v1, p1, v2) only.  A tied maximum shows as v1 == v2 after
+// the warp reduction; only then is the row scanned again with exact tie
+// tracking (scan_row).  Within a 16-byte chunk the top-2 is a pairwise tree of
+// independent min/max operations; only the merge into the lane state is serial.
+template <typename R, int W>
+__device__ __forceinline__ void chunk_top2(const R* v, R& mx, R& sd, int& ix) {
+    R m[W], n[W];
+    int i[W];
+#pragma unroll
+    for (int e = 0; e < W; ++e) { m[e] = v[e]; n[e] = -INFINITY; i[e] = e; }
+#pragma unroll
+    for (int w = W; w > 1; w >>= 1) {
+#pragma unroll
+        for (int e = 0; e < w / 2; ++e) {
+            const R a = m[2 * e], b = m[2 * e + 1];
+            const bool right = b > a;  // ties keep the earlier column
+            const R nn = rmax(rmin(a, b), rmax(n[2 * e], n[2 * e + 1]));
+            i[e] = right ? i[2 * e + 1] : i[2 * e];
+            m[e] = rmax(a, b);
+            n[e] = nn;
+        }
+    }
+    mx = m[0]; sd = n[0]; ix = i[0];
+}
+
+template <typename R>
+__device__ __forceinline__ void lane_merge(Top2<R>& t, R mx, R sd, int col) {
+    const bool gt = (mx > t.v1) || (t.p1 < 0);
+    t.v2 = gt ? rmax(t.v1, sd) : rmax(t.v2, mx);
+    t.p1 = gt ? col : t.p1;
+    t.v1 = gt ? mx : t.v1;
+}
+
+template <typename In, typename R, int UNROLL>
+__device__ __forceinline__ void scan_chunks_fast(const uint4* rv, const R* __restrict__ Ps, int base, int stride,
+                                                 int nchunks, Top2<R>& t) {
+    constexpr int W = Elem<In>::W;
+    for (; base < nchunks; base += stride * UNROLL) {
+        uint4 raw[UNROLL];
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int ch = base + u * stride;
+            if (ch < nchunks) raw[u] = ld_stream16(rv + ch);
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int ch = base + u * stride;
+            if (ch < nchunks) {
+                R x[W], pr[W], v[W];
+                Elem<In>::template unpack<R>(raw[u], x);
+                load_prices<R, W>(Ps, ch * W, pr);
+#pragma unroll
+                for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
+                R mx, sd;
+                int ix;
+                chunk_top2<R, W>(v, mx, sd, ix);
+                lane_merge(t, mx, sd, ch * W + ix);
+            }
+        }
+    }
+}
+
+// Warp reduction of fast states; p2 stays -1 (v1 == v2 marks a tie).
+template <typename R> __device__ __forceinline__ Top2<R> top2_warp_fast(Top2<R> t) {
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+        Top2<R> o;
+        o.v1 = __shfl_xor_sync(0xffffffffu, t.v1, off);
+        o.v2 = __shfl_xor_sync(0xffffffffu, t.v2, off);
+        o.p1 = __shfl_xor_sync(0xffffffffu, t.p1, off);
+        if (o.p1 >= 0) {
+            if (t.p1 < 0) { t = o; }
+            else {
+                const bool ob = (o.v1 > t.v1) || (o.v1 == t.v1 && o.p1 < t.p1);
+                const R lo = ob ? t.v1 : o.v1;
+                t.v2 = rmax(rmax(t.v2, o.v2), lo);
+                if (ob) { t.v1 = o.v1; t.p1 = o.p1; }
+            }
+        }
+    }
+    t.p2 = -1;
+    return t;
+}
+template <> __device__ __forceinline__ Top2<float> top2_warp_fast<float>(Top2<float> t) {
+    const int big = 0x7fffffff;
+    const bool live = t.p1 >= 0;
+    const unsigned int k1 = live ? fkey(t.v1) : 0u;
+    const unsigned int K1 = __reduce_max_sync(0xffffffffu, k1);
+    const bool top = live && k1 == K1;
+    const int P1 = (int)__reduce_min_sync(0xffffffffu, (unsigned int)(top ? t.p1 : big));
+    // second value: a second lane at the maximum, the top lane's own second,
+    // or the best other lane
+    const unsigned int k2 = !live ? 0u : ((top && t.p1 == P1) ? (t.v2 == -INFINITY ? 0u : fkey(t.v2)) : k1);
+    const unsigned int K2 = __reduce_max_sync(0xffffffffu, k2);
+    Top2<float> r;
+    r.p1 = (K1 == 0u) ? -1 : P1;
+    r.v1 = (K1 == 0u) ? -INFINITY : fkey_inv(K1);
+    r.v2 = (K2 == 0u) ? -INFINITY : fkey_inv(K2);
+    r.p2 = -1;
+    return r;
+}
+
+template <typename In, typename R, int UNROLL>
+__device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row, const R* __restrict__ Ps,
+                                                 int lane, int sub, int wpr) {
+    const int M = (int)p.M;
+    Top2<R> t;
+    top2_init(t);
+    if (p.vec_ok) {
+        constexpr int W = Elem<In>::W;
+        const int nchunks = M / W;
+        const int stride = 32 * wpr;
+        const int per_lane = (nchunks + stride - 1) / stride;
+        const uint4* rv = reinterpret_cast<const uint4*>(row);
+        const int base = sub * 32 + lane;
+        if (per_lane <= 1) scan_chunks_fast<In, R, 1>(rv, Ps, base, stride, nchunks, t);
+        else if (per_lane <= 2) scan_chunks_fast<In, R, 2>(rv, Ps, base, stride, nchunks, t);
+        else if (per_lane <= 4 || UNROLL <= 4) scan_chunks_fast<In, R, 4>(rv, Ps, base, stride, nchunks, t);
+        else scan_chunks_fast<In, R, UNROLL>(rv, Ps, base, stride, nchunks, t);
+    } else {
+        for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
+            lane_merge(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), (R)-INFINITY, col);
+    }
+    return top2_warp_fast(t);
+}
+
 // Top-2 over the columns of one row that this warp covers: the row's 16-byte
 // chunks are dealt to `wpr` warps in turn (warp `sub` takes chunks
 // sub*32+lane, sub*32+lane+32*wpr, ...).  The batch size follows the number
 // of chunks per lane, so no predicated-off batch slots are issued.  The
 // result is reduced over the warp.
 template <typename In, typename R, int UNROLL>
-__device__ __forceinline__ Top2<R> scan_row(const Params& p, const In* row, const R* __restrict__ Ps,
-                                            int lane, int sub, int wpr) {
+__device__ __noinline__ Top2<R> scan_row(const Params& p, const In* row, const R* __restrict__ Ps,
+                                         int lane, int sub, int wpr) {
     const int M = (int)p.M;
     Top2<R> t;
     top2_init(t);
@@ -508,6 +649,20 @@ __device__ __forceinline__ void put_entry(unsigned long long* seg, int k, unsign
     if (Ex<R>::EW == 3) st_relaxed_u64(w + 2, tag | (bits >> 32));
 }
 
+template <typename R>
+__device__ __forceinline__ bool entry_tags_ok(const unsigned long long* w, unsigned int t1) {
+    if ((w[0] >> 48) != (t1 & 0xffffu) || (unsigned int)(w[1] >> 32) != t1) return false;
+    return Ex<R>::EW == 2 || (unsigned int)(w[2] >> 32) == t1;
+}
+template <typename R>
+__device__ __forceinline__ void decode_entry(const unsigned long long* w, int& row, int& col, R& bid) {
+    row = (int)((w[0] >> 24) & 0xffffffull);
+    col = (int)(w[0] & 0xffffffull);
+    const unsigned long long hi = (Ex<R>::EW == 3) ? w[2] : 0ull;
+    const unsigned long long bits = (w[1] & 0xffffffffull) | ((hi & 0xffffffffull) << 32);
+    bid = Bits<R>::from((typename Bits<R>::U)bits);
+}
+
 // One attempt to read entry k; false if some word is not yet from round t1.
 template <typename R>
 __device__ __forceinline__ bool get_entry(const unsigned long long* seg, int k, unsigned int t1, int& row, int& col,
@@ -553,16 +708,20 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
     return L;
 }
 
-// Launch shapes: one CTA per problem runs 256 threads at up to 4 CTAs per SM
+// Launch shapes: one CTA per problem runs 256 threads at up to 2 CTAs per SM
 // (a batch of small problems stays in one wave); the multi-CTA path runs 512
 // threads, one CTA per SM.
 #define ELA_THREADS_ONE 256
-#define ELA_MINB_ONE 4
+#ifndef ELA_MINB_ONE
+#define ELA_MINB_ONE 2
+#endif
+#ifndef ELA_UNROLL_ONE
 #define ELA_UNROLL_ONE 4
+#endif
 #define ELA_THREADS_MULTI 512
 #define ELA_MINB_MULTI 1
 #ifndef ELA_UNROLL_MULTI
-#define ELA_UNROLL_MULTI 8
+#define ELA_UNROLL_MULTI 4
 #endif
 #define ELA_MAX_S 256
 #define ELA_WS_HEADER 256
@@ -571,7 +730,8 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 // row within 1e-5 of it wins -> owners of bid-on columns are evicted.
 //   MULTI == false: every CTA solves whole problems (blockIdx.x, +gridDim.x, ...);
 //                   a round's bids go straight into the CTA's shared list.
-//   MULTI == true:  S CTAs share a problem; CTA c owns rows c, c+S, c+2S, ...
+//   MULTI == true:  S CTAs share a problem; CTA c owns the block of rows
+//                   [c*rpc, (c+1)*rpc), rpc = ceil(N/S) (few TLB pages per CTA)
 template <typename In, typename R, bool MULTI, int THREADS, int MINB, int UNROLL>
 __global__ void __launch_bounds__(THREADS, MINB)
 auction_kernel(const Params p) {
@@ -586,7 +746,8 @@ auction_kernel(const Params p) {
     const int S = MULTI ? p.S : 1;
     const int g = blockIdx.x / S, c = blockIdx.x % S;
     const int N = (int)p.N, M = (int)p.M;
-    const int my_rows = (c < N) ? (N - 1 - c) / S + 1 : 0;  // rows c, c+S, ...
+    const int row0 = c * p.rows_per_cta;                           // first owned row
+    const int my_rows = (row0 < N) ? min(p.rows_per_cta, N - row0) : 0;
     const KLayout L = k_layout<R>(N, M, p.rows_per_cta, nw);
     R* P = reinterpret_cast<R*>(smem + L.P);
     U* maxb = reinterpret_cast<U*>(smem + L.maxb);
@@ -615,23 +776,29 @@ auction_kernel(const Params p) {
         for (int q = tid; q < my_rows; q += blockDim.x) { rowcol[q] = -1; rowbid[q] = -1; }
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
+        bool rebuild = true;  // the active list is rebuilt from rowcol at problem and epsilon starts
         __syncthreads();
         while (ph < p.n_eps) {
             if (it == p.max_iter) {  // round budget of this epsilon used up
                 if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
                 it = 0;
+                rebuild = true;
                 __syncthreads();
                 continue;
             }
             const R eps = (R)p.eps[ph];
             const unsigned int t1 = t + 1;
             PROF_MARK(pt0);
-            // ---- own rows that bid this round
-            if (tid == 0) { s_nact = 0; s_total = 0; s_extra = 0; s_fail = 0; }
-            __syncthreads();
-            for (int q = tid; q < my_rows; q += blockDim.x)
-                if (rowcol[q] < 0) active[atomicAdd(&s_nact, 1)] = q;
+            // ---- own rows that bid this round (otherwise listed by the last election)
+            if (rebuild) {
+                if (tid == 0) s_nact = 0;
+                __syncthreads();
+                for (int q = tid; q < my_rows; q += blockDim.x)
+                    if (rowcol[q] < 0) active[atomicAdd(&s_nact, 1)] = q;
+                rebuild = false;
+            }
+            if (tid == 0) { s_total = 0; s_extra = 0; s_fail = 0; }
             __syncthreads();
             const int K = s_nact;
             PROF_MARK(pt1);
@@ -640,40 +807,78 @@ auction_kernel(const Params p) {
             // ---- bids against the round-start prices.  With few rows, a row is
             //      dealt to several warps so that its scan is one memory latency.
             if (K > 0) {
-                int wpr = 1;
+                // warps per row: the largest power of two with wpr * K <= nw
+                // (nw is a power of two), as a shift
+                int lw = 0;
                 if (M >= 1024 && K < nw) {
-                    wpr = nw / K;
-                    while (wpr & (wpr - 1)) wpr &= wpr - 1;  // power of two
+                    const int lnw = 31 - __clz(nw);
+                    const int lk = (K > 1) ? 32 - __clz(K - 1) : 0;  // ceil(log2 K)
+                    lw = lnw - lk;
+                    const int lmax = 31 - __clz(p.max_wpr);
+                    if (lw > lmax) lw = lmax;
                 }
-                const int groups = nw / wpr;
+                const int wpr = 1 << lw;
+                const int groups = nw >> lw;
                 for (int kb = 0; kb < K; kb += groups) {
-                    const int k = kb + warp / wpr, sub = warp % wpr;
+                    const int k = kb + (warp >> lw), sub = warp & (wpr - 1);
                     const bool has = k < K;
                     const int q = has ? active[k] : 0;
-                    const int i = c + q * S;
+                    const int i = row0 + q;
                     const In* row = base + (int64_t)i * p.stride_n;
                     Top2<R> tt;
                     top2_init(tt);
-#ifdef ELA_SCAN_TWICE
-                    if (has) { long long q0 = clock64(); tt = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
-                               if (lane == 0 && t < 8192) atomicMax(&g_trace[t][4], (unsigned long long)(clock64() - q0)); }
+#ifdef ELA_PROF_SPLIT
+                    if (has && wpr == 16 && p.vec_ok) {
+                        constexpr int W = Elem<In>::W;
+                        long long d[2];
+                        const long long a00 = clock64();
+                        for (int rep = 0; rep < 2; ++rep) {
+                            const long long a0 = clock64();
+                            Top2<R> t0; top2_init(t0);
+                            scan_chunks_fast<In, R, 2>(reinterpret_cast<const uint4*>(row), P, sub * 32 + lane, 512, M / W, t0);
+                            tt = top2_warp_fast(t0);
+                            d[rep] = clock64() - a0;
+                        }
+                        if (warp == 0 && lane == 0 && t < 8192) { g_trace[t][11] = a00 - pt1; g_trace[t][7] = d[0]; g_trace[t][4] = d[1]; }
+                    } else
 #endif
-                    PROF_MARK(ps0);
-                    if (has) tt = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                    if (has) tt = scan_row_fast<In, R, UNROLL>(p, row, P, lane, sub, wpr);
 #ifdef ELA_PROF
-                    { long long ps1 = clock64();
-                      if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][7], (unsigned long long)(ps1 - ps0)); }
+                    if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][8], (unsigned long long)(clock64() - pt1));
 #endif
+                    // exact tie tracking is needed only when the maximum is tied
+                    // and M >= 128 (below that the tie is settled by introselect)
+                    const bool exact_ok = M >= ELA_SMALL_M;
                     if (wpr > 1) {
                         if (has && lane == 0) wtop[warp] = tt;
                         __syncthreads();
-                        if (has && sub == 0) {  // lanes fetch the group's partial results; butterfly merge
+                        const int gb = warp - sub;  // first warp of this row's group
+                        if (has) {  // every warp of the group merges the group's partial results
                             Top2<R> o;
                             top2_init(o);
-                            if (lane < wpr) o = wtop[warp + lane];
-                            tt = top2_warp(o);
+                            if (lane < wpr) o = wtop[gb + lane];
+                            tt = top2_warp_fast(o);
                         }
+                        const bool rowtie = exact_ok && has && tt.v1 == tt.v2;
+                        if (__syncthreads_or(rowtie)) {  // also orders the wtop reads before rewrites
+                            Top2<R> ex;
+                            top2_init(ex);
+                            if (rowtie) ex = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                            if (rowtie && lane == 0) wtop[warp] = ex;
+                            __syncthreads();
+                            if (rowtie && sub == 0) {
+                                Top2<R> o;
+                                top2_init(o);
+                                if (lane < wpr) o = wtop[gb + lane];
+                                tt = top2_warp(o);
+                            }
+                        }
+                    } else if (exact_ok && has && tt.v1 == tt.v2) {
+                        tt = scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1);
                     }
+#ifdef ELA_PROF
+                    if (has && sub == 0 && lane == 0 && t < 8192) atomicMax(&g_trace[t][9], (unsigned long long)(clock64() - pt1));
+#endif
                     if (has && sub == 0) {
                         int j1;
                         R bid;
@@ -682,9 +887,12 @@ auction_kernel(const Params p) {
                             rowbid[q] = j1;
                             if (!MULTI) { lbid[k] = bid; lrow[k] = i; lcol[k] = j1; }
                             else put_entry<R>(myseg, k, t1, i, j1, bid);
+#ifdef ELA_PROF
+                            if (t < 8192) atomicMax(&g_trace[t][10], (unsigned long long)(clock64() - pt1));
+#endif
                         }
                     }
-                    if (wpr > 1) __syncthreads();
+                    if (wpr > 1 && kb + groups < K) __syncthreads();  // wtop is reused
                 }
             }
             __syncthreads();
@@ -703,9 +911,19 @@ auction_kernel(const Params p) {
                     const unsigned long long t0 = globaltimer_ns();
                     unsigned int spins = 0;
                     int cntv = -1;
-                    for (;;) {  // bounded wait for the segment's header
-                        const unsigned long long h = ld_relaxed_u64(seg);
-                        if ((unsigned int)(h >> 32) == t1) { cntv = (int)(unsigned int)(h & 0xffffffffull); break; }
+                    constexpr int NW = 1 + Ex<R>::INL * Ex<R>::EW;
+                    unsigned long long w[NW];
+                    for (;;) {  // bounded wait: header and inline entries, loaded together
+#pragma unroll
+                        for (int k = 0; k < NW; ++k) w[k] = ld_relaxed_u64(seg + k);
+                        if ((unsigned int)(w[0] >> 32) == t1) {
+                            const int cn = (int)(unsigned int)(w[0] & 0xffffffffull);
+                            bool ok = true;
+#pragma unroll
+                            for (int k = 0; k < Ex<R>::INL; ++k)
+                                if (k < cn) ok = ok && entry_tags_ok<R>(w + 1 + Ex<R>::EW * k, t1);
+                            if (ok) { cntv = cn; break; }
+                        }
 #ifdef ELA_POLL_SLEEP
                         __nanosleep(ELA_POLL_SLEEP);
 #endif
@@ -725,21 +943,14 @@ auction_kernel(const Params p) {
                         s_cnt[tid] = cntv;
                         s_off[tid] = off;
                         if (cntv > Ex<R>::INL) s_extra = 1;
-                        const int ninl = cntv < Ex<R>::INL ? cntv : Ex<R>::INL;
-                        for (int k = 0; k < ninl; ++k) {
-                            int rr = 0, cc = 0;
-                            R bb = (R)0;
-                            unsigned int tries = 0;
-                            while (!get_entry<R>(seg, k, t1, rr, cc, bb)) {
-                                if (++tries > (1u << 22)) {
-                                    s_fail = 1;
-                                    atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
-                                    atomicExch(abort_flag, 1);
-                                    break;
-                                }
+#pragma unroll
+                        for (int k = 0; k < Ex<R>::INL; ++k)
+                            if (k < cntv) {
+                                int rr, cc;
+                                R bb;
+                                decode_entry<R>(w + 1 + Ex<R>::EW * k, rr, cc, bb);
+                                lbid[off + k] = bb; lrow[off + k] = rr; lcol[off + k] = cc;
                             }
-                            lbid[off + k] = bb; lrow[off + k] = rr; lcol[off + k] = cc;
-                        }
                     }
                 }
                 __syncthreads();
@@ -775,6 +986,7 @@ auction_kernel(const Params p) {
             ++t;
             PROF_MARK(pt3);
             if (ntot == 0) {  // nobody bid: this epsilon's solve has converged
+                rebuild = true;
                 if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
                 it = 0;
@@ -785,6 +997,7 @@ auction_kernel(const Params p) {
             rowbids += ntot;
             // ---- election, identical in every CTA of the group
             for (int e = tid; e < ntot; e += blockDim.x) atomicMax(&maxb[lcol[e]], BT::to(lbid[e]));
+            if (tid == 0) s_nact = 0;
             __syncthreads();
             for (int e = tid; e < ntot; e += blockDim.x) {
                 const int j = lcol[e];
@@ -793,19 +1006,22 @@ auction_kernel(const Params p) {
             __syncthreads();
             for (int q = tid; q < my_rows; q += blockDim.x) {
                 const int jb = rowbid[q];
+                int col = rowcol[q];
                 if (jb >= 0) {
-                    rowcol[q] = (win[jb] == c + q * S + 1) ? jb : -1;
+                    col = (win[jb] == row0 + q + 1) ? jb : -1;
                     rowbid[q] = -1;
-                } else {
-                    const int j = rowcol[q];
-                    if (j >= 0 && maxb[j] != 0) rowcol[q] = -1;  // someone took the column
+                } else if (col >= 0 && maxb[col] != 0) {
+                    col = -1;  // someone took the column
                 }
+                rowcol[q] = col;
+                if (col < 0) active[atomicAdd(&s_nact, 1)] = q;  // bids next round
             }
             for (int e = tid; e < ntot; e += blockDim.x) P[lcol[e]] = BT::from(maxb[lcol[e]]);
             __syncthreads();
+            // cleared before the next round's election; the bid phase's
+            // barriers lie in between
             for (int e = tid; e < ntot; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
             ++it;
-            __syncthreads();
             PROF_MARK(pt4);
             PROF_ADD(0, pt0, pt1); PROF_ADD(1, pt1, pt2); PROF_ADD(2, pt2, pt3); PROF_ADD(3, pt3, pt4);
             PROF_ADD(4, 0, 1); PROF_ADD(5, 0, (K > 0));
@@ -819,7 +1035,7 @@ auction_kernel(const Params p) {
                 if (blockIdx.x == 0 && threadIdx.x == 0) {
                     g_trace[t - 1][0] = ntot; g_trace[t - 1][1] = pt1 - pt0; g_trace[t - 1][2] = pt2 - pt1;
                     g_trace[t - 1][3] = pt3 - pt2;
-#ifndef ELA_SCAN_TWICE
+#if !defined(ELA_SCAN_TWICE) && !defined(ELA_PROF_SPLIT)
                     g_trace[t - 1][4] = pt4 - pt3;
 #endif
                 }
@@ -832,7 +1048,7 @@ auction_kernel(const Params p) {
         int mine = 0;
         for (int q = tid; q < my_rows; q += blockDim.x) {
             const int a = rowcol[q];
-            p.assign_out[b * p.N + c + (int64_t)q * S] = a;
+            p.assign_out[b * p.N + row0 + q] = a;
             mine += (a < 0);
         }
         if (mine) atomicAdd(&s_unassigned, mine);
@@ -1000,6 +1216,11 @@ int fill_params(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, in
     p.stats_out = stats_out;
     p.wait_ns = g_wait_ns;
     p.skip_publish = g_skip_publish;
+    p.max_wpr = 32;
+    if (const char* env = getenv("ELA_MAX_WARPS_PER_ROW")) {  // tuning knob
+        const int v = atoi(env);
+        if (v >= 1) p.max_wpr = v;
+    }
     return ELA_OK;
 }
 
