@@ -5,8 +5,8 @@ hand-written sm_100a CUDA kernels behind a C ABI (include/ela_auction.h).
 """
 from .api import BACKENDS, AuctionIMLE, linear_assignment
 from .solver import AuctionB200, auction_solve_op, solve
-from ._lib import AuctionError, PATH_AUTO, PATH_CTA, PATH_GRID
+from ._lib import AuctionError, PATH_AUTO, PATH_CTA, PATH_GRID, PATH_CLUSTER
 from . import workloads
 
 __all__ = ["linear_assignment", "AuctionIMLE", "AuctionB200", "BACKENDS", "solve",
-           "auction_solve_op", "AuctionError", "PATH_AUTO", "PATH_CTA", "PATH_GRID", "workloads"]
+           "auction_solve_op", "AuctionError", "PATH_AUTO", "PATH_CTA", "PATH_GRID", "PATH_CLUSTER", "workloads"]

@@ -18,7 +18,7 @@ ELA_ERR_TIMEOUT = 3
 ELA_ERR_UNSUPPORTED = 4
 ELA_ERR_INTERNAL = 5
 
-PATH_AUTO, PATH_CTA, PATH_GRID = 0, 1, 2
+PATH_AUTO, PATH_CTA, PATH_GRID, PATH_CLUSTER = 0, 1, 2, 3
 
 # Every symbol include/ela_auction.h declares, with (restype, argtypes).
 _c = ctypes

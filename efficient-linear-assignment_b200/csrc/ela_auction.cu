@@ -21,9 +21,11 @@
 // The C ABI is declared in include/ela_auction.h.
 
 #include <cuda_runtime.h>
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cuda_bf16.h>
 #include <stdint.h>
+#include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -380,6 +382,8 @@ struct Params {
     unsigned long long wait_ns;
     int skip_publish;        // test hook: CTA 0 never publishes its first round
     int max_wpr;             // most warps that share one row's scan (power of two)
+    int team;                // cluster path: clusters per problem
+    size_t team_bytes;       // cluster path: workspace bytes per team
 };
 
 // ------------------------------------------------------------ row scanning
@@ -633,6 +637,14 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* ptr, unsigned long long v) {
     asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }
+__device__ __forceinline__ void st_release_u32(unsigned int* ptr, unsigned int v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int* ptr) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -678,6 +690,57 @@ __device__ __forceinline__ bool get_entry(const unsigned long long* seg, int k, 
     const unsigned long long bits = (lo & 0xffffffffull) | ((hi & 0xffffffffull) << 32);
     bid = Bits<R>::from((typename Bits<R>::U)bits);
     return true;
+}
+
+
+// Reads every entry past the inline ones of the S segments of round t1,
+// spread over the whole CTA (one L2 latency, not one per segment).  cnt/off:
+// per-segment counts and list offsets; exoff: S+1 ints of shared scratch.
+// Returns false if an entry never showed up (status and abort flag are set).
+template <typename R>
+__device__ bool read_extra_entries(const unsigned char* segbase, size_t seg_bytes, int S, const int* cnt,
+                                   const int* off, int* exoff, unsigned int t1, R* lbid, int* lrow, int* lcol,
+                                   int* abort_flag, int32_t* status) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < 32) {  // exclusive prefix of the extra counts, one warp
+        const int per = (S + 31) / 32, a = lane * per, b = min(S, a + per);
+        int sum = 0;
+        for (int sg = a; sg < b; ++sg) sum += max(0, cnt[sg] - Ex<R>::INL);
+        int x = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        int run = x - sum;
+        for (int sg = a; sg < b; ++sg) { exoff[sg] = run; run += max(0, cnt[sg] - Ex<R>::INL); }
+        if (lane == 31) exoff[S] = x;
+    }
+    __syncthreads();
+    const int total = exoff[S];
+    bool ok = true;
+    for (int idx = tid; idx < total && ok; idx += blockDim.x) {
+        int lo = 0, hi = S - 1;  // last segment whose extra entries start at or before idx
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (exoff[mid] <= idx) lo = mid; else hi = mid - 1;
+        }
+        const int k = Ex<R>::INL + (idx - exoff[lo]);
+        const unsigned long long* seg = reinterpret_cast<const unsigned long long*>(segbase + (size_t)lo * seg_bytes);
+        int rr = 0, cc = 0;
+        R bb = (R)0;
+        unsigned int tries = 0;
+        while (!get_entry<R>(seg, k, t1, rr, cc, bb)) {
+            if (++tries > (1u << 22)) {
+                atomicCAS(status, ELA_OK, ELA_ERR_TIMEOUT);
+                atomicExch(abort_flag, 1);
+                ok = false;
+                break;
+            }
+        }
+        lbid[off[lo] + k] = bb; lrow[off[lo] + k] = rr; lcol[off[lo] + k] = cc;
+    }
+    return __syncthreads_and(ok) != 0;
 }
 
 // ================================================================== kernel
@@ -740,6 +803,7 @@ auction_kernel(const Params p) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_nact, s_total, s_extra, s_fail;
     __shared__ int s_cnt[MULTI ? ELA_MAX_S : 1], s_off[MULTI ? ELA_MAX_S : 1];
+    __shared__ int s_exoff[MULTI ? ELA_MAX_S + 1 : 1];
     __shared__ int s_unassigned;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
@@ -958,28 +1022,9 @@ auction_kernel(const Params p) {
                 PROF_ADDALL(8, pt2b - pt2);
                 if (s_fail) return;
                 if (s_extra) {  // rounds with many bids: read the remaining entries together
-                    for (int sg = 0; sg < S; ++sg) {
-                        const int cn = s_cnt[sg];
-                        if (cn <= Ex<R>::INL) continue;
-                        const unsigned long long* seg =
-                            reinterpret_cast<const unsigned long long*>(gbase + (size_t)((t & 1) * S + sg) * p.seg_bytes);
-                        for (int k = Ex<R>::INL + tid; k < cn; k += blockDim.x) {
-                            int rr = 0, cc = 0;
-                            R bb = (R)0;
-                            unsigned int tries = 0;
-                            while (!get_entry<R>(seg, k, t1, rr, cc, bb)) {
-                                if (++tries > (1u << 22)) {
-                                    s_fail = 1;
-                                    atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
-                                    atomicExch(abort_flag, 1);
-                                    break;
-                                }
-                            }
-                            lbid[s_off[sg] + k] = bb; lrow[s_off[sg] + k] = rr; lcol[s_off[sg] + k] = cc;
-                        }
-                    }
-                    __syncthreads();
-                    if (s_fail) return;
+                    if (!read_extra_entries<R>(gbase + (size_t)((t & 1) * S) * p.seg_bytes, p.seg_bytes, S, s_cnt,
+                                               s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag, p.status))
+                        return;
                 }
                 ntot = s_total;
             }
@@ -1070,6 +1115,527 @@ auction_kernel(const Params p) {
     }
 }
 
+
+// ============================================================ cluster kernel
+// One thread-block cluster (CS CTAs, CS = 16 where the device allows it, else
+// 8) per problem.  Every CTA holds the whole problem state in shared memory
+// (prices, column owners, row assignments) and replays every round's election
+// identically; the CTAs of the cluster exchange data through distributed
+// shared memory (stores into the other CTAs' shared memory) and the cluster
+// barrier.  Two kinds of rounds:
+//   large rounds (K > ELA_SMALL_ROUND rows bid): each CTA scans its own block
+//     of rows in full and stores its bids into every CTA's bid list;
+//   small rounds: every CTA scans its 1/CS slice of the columns of all K
+//     active rows and stores a partial top-2 per row into every CTA; each CTA
+//     merges the CS partials of a row (the merge is exact, ties included), so
+//     a row costs one memory latency instead of a full-row scan.
+// The number of active rows never grows within an epsilon, so a solve runs
+// large rounds, then small rounds, per epsilon.
+// Per round: [scan] wait(consumed) [store to all CTAs] arrive+wait(ready)
+// [merge, election] arrive(consumed).  The second barrier phase lets a CTA
+// store the next round's data only after every CTA has read this round's.
+
+#define ELA_SMALL_ROUND 64
+
+struct CLayout {
+    size_t P, maxb, win, owner, rowcol, act, lbid, lrow, lcol, part, cnt, evict, total;
+};
+template <typename R>
+__host__ __device__ inline CLayout c_layout(int64_t N, int64_t M, int CS) {
+    CLayout L;
+    const int rpc = (int)((N + CS - 1) / CS);
+    const size_t nlist = (size_t)rpc * CS;  // slot rank*rpc + k
+    size_t o = 0;
+    L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);
+    L.maxb = o;   o = align_up(o + sizeof(R) * (size_t)M, 16);
+    L.win = o;    o = align_up(o + 4 * (size_t)M, 16);
+    L.owner = o;  o = align_up(o + 4 * (size_t)M, 16);
+    L.rowcol = o; o = align_up(o + 4 * (size_t)N, 16);
+    L.act = o;    o = align_up(o + 4 * (size_t)N, 16);
+    L.lbid = o;   o = align_up(o + sizeof(R) * nlist, 16);
+    L.lrow = o;   o = align_up(o + 4 * nlist, 16);
+    L.lcol = o;   o = align_up(o + 4 * nlist, 16);
+    L.part = o;   o = align_up(o + sizeof(Top2<R>) * (size_t)CS * ELA_SMALL_ROUND, 16);
+    L.cnt = o;    o = align_up(o + 4 * (size_t)CS, 16);
+    L.evict = o;  o = align_up(o + 4 * (size_t)ELA_SMALL_ROUND, 16);
+    L.total = o;
+    return L;
+}
+
+__device__ __forceinline__ void cluster_arrive_release() {
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Block-wide ordered compaction of the rows with rowcol < 0 into act[];
+// returns the count (all threads).  Deterministic: ascending row order.
+__device__ int compact_unassigned(const int* rowcol, int N, int* act, int* s_scan) {
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+    const int chunk = (N + nt - 1) / nt;
+    const int r0 = tid * chunk, r1 = min(N, r0 + chunk);
+    int mine = 0;
+    for (int i = r0; i < r1; ++i) mine += (rowcol[i] < 0);
+    // exclusive scan of `mine` over the block
+    int x = mine;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, x, off);
+        if (lane >= off) x += y;
+    }
+    if (lane == 31) s_scan[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+        int w = (lane < nw) ? s_scan[lane] : 0;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, w, off);
+            if (lane >= off) w += y;
+        }
+        if (lane < nw) s_scan[lane] = w;  // inclusive warp totals
+    }
+    __syncthreads();
+    int pos = x - mine + (warp > 0 ? s_scan[warp - 1] : 0);
+    for (int i = r0; i < r1; ++i)
+        if (rowcol[i] < 0) act[pos++] = i;
+    const int total = s_scan[nw - 1];
+    __syncthreads();
+    return total;
+}
+
+// Team layout: ngroups teams of p.team clusters; a team solves one problem at
+// a time.  Large rounds use every CTA of the team (rows split over the team;
+// bids exchanged through distributed shared memory when the team is one
+// cluster, through tagged words in global memory otherwise).  Small rounds
+// run in the team's first (leader) cluster only; the other clusters wait for
+// the end of the epsilon and then reload the prices the leader publishes.
+// Per-team workspace: [2 x ST exchange segments][prices M][flag word].
+template <typename In, typename R>
+__global__ void __launch_bounds__(ELA_THREADS_MULTI, 1)
+auction_cluster_kernel(const Params p) {
+    namespace cg = cooperative_groups;
+    typedef Bits<R> BT;
+    typedef typename BT::U U;
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int s_scan[32];
+    __shared__ int s_cnt, s_total, s_extra, s_fail;
+    __shared__ int s_off[ELA_MAX_S + 1];
+    __shared__ int s_segcnt[ELA_MAX_S];
+    __shared__ int s_exoff[ELA_MAX_S + 1];
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int CS = (int)cluster.num_blocks();
+    const int rank = (int)cluster.block_rank();
+    const int cid = blockIdx.x / CS;
+    const int TC = p.team;                    // clusters per team
+    const int team = cid / TC, tc = cid % TC;
+    const bool leader = (tc == 0);
+    const int ST = TC * CS;                   // CTAs per team
+    const int gi = tc * CS + rank;            // this CTA within the team
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int N = (int)p.N, M = (int)p.M;
+    constexpr int W = Elem<In>::W;
+    const int nchunks = M / W;
+    const int rpc = (N + ST - 1) / ST;        // large rounds: rows per CTA
+    const int row0 = gi * rpc, my_rows = max(0, min(rpc, N - row0));
+    const CLayout L = c_layout<R>(N, M, CS);
+    R* P = reinterpret_cast<R*>(smem + L.P);
+    U* maxb = reinterpret_cast<U*>(smem + L.maxb);
+    int* win = reinterpret_cast<int*>(smem + L.win);
+    int* owner = reinterpret_cast<int*>(smem + L.owner);
+    int* rowcol = reinterpret_cast<int*>(smem + L.rowcol);
+    int* act = reinterpret_cast<int*>(smem + L.act);
+    R* lbid = reinterpret_cast<R*>(smem + L.lbid);
+    int* lrow = reinterpret_cast<int*>(smem + L.lrow);
+    int* lcol = reinterpret_cast<int*>(smem + L.lcol);
+    Top2<R>* part = reinterpret_cast<Top2<R>*>(smem + L.part);
+    int* cnt = reinterpret_cast<int*>(smem + L.cnt);
+    int* evict = reinterpret_cast<int*>(smem + L.evict);
+    const R tol = (R)1e-5;
+    // small rounds: the slice of the columns this CTA scans (16-byte chunks)
+    const int per = (nchunks + CS - 1) / CS;
+    const int ch0 = rank * per, ch1 = min(nchunks, ch0 + per);
+    const bool small_ok = (M >= 1024);
+    // global memory of this team (only used when TC > 1)
+    int* abort_flag = reinterpret_cast<int*>(p.ws);
+    unsigned char* tb = p.ws + ELA_WS_HEADER + (size_t)team * p.team_bytes;
+    R* pbuf = reinterpret_cast<R*>(tb + 2 * (size_t)ST * p.seg_bytes);
+    unsigned int* pflag = reinterpret_cast<unsigned int*>(tb + 2 * (size_t)ST * p.seg_bytes + align_up(sizeof(R) * (size_t)M, 256));
+
+    bool cl_pending = false;      // a "consumed" arrival on the cluster barrier awaits its wait
+    unsigned int t = 0;           // global-exchange round tag (large rounds, TC > 1)
+    unsigned int seq = 0;         // epsilons the leader has published (TC > 1)
+    cluster.sync();               // every CTA of the cluster runs before any remote store
+
+    for (int64_t b = team; b < p.B; b += p.ngroups) {
+        const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
+        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; maxb[j] = 0; win[j] = 0; owner[j] = -1; }
+        for (int i = tid; i < N; i += blockDim.x) rowcol[i] = -1;
+        long long rounds = 0, rowbids = 0;
+        int ph = 0, it = 0;
+        __syncthreads();
+        int K = N;  // rows that bid this round (every CTA of the team agrees)
+        bool small = small_ok && K <= ELA_SMALL_ROUND;
+        if (small) K = compact_unassigned(rowcol, N, act, s_scan);
+        while (ph < p.n_eps) {
+            if (it == p.max_iter || K == 0) {  // this epsilon is done
+                if (small && TC > 1) {
+                    // the leader publishes its prices; the other clusters wait for them
+                    ++seq;
+                    if (leader) {
+                        if (rank == 0) {
+                            for (int j = tid; j < M; j += blockDim.x) __stcg(pbuf + j, P[j]);
+                            __threadfence();
+                            __syncthreads();
+                            if (tid == 0) st_release_u32(pflag, seq);
+                        }
+                    } else {
+                        if (tid == 0) {
+                            const unsigned long long t0 = globaltimer_ns();
+                            int ok = 1;
+                            unsigned int spins = 0;
+                            while (ld_acquire_u32(pflag) < seq) {
+                                if ((++spins & 63u) == 0) {
+                                    if (*(volatile int*)abort_flag) { ok = 0; break; }
+                                    if (globaltimer_ns() - t0 > p.wait_ns) {
+                                        atomicExch(abort_flag, 1);
+                                        atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                                        ok = 0;
+                                        break;
+                                    }
+                                }
+                            }
+                            s_fail = !ok;
+                        }
+                        __syncthreads();
+                        if (s_fail) { if (cl_pending) cluster_wait_acquire(); cluster.sync(); return; }
+                        for (int j = tid; j < M; j += blockDim.x) P[j] = __ldcg(pbuf + j);
+                    }
+                }
+                if (++ph >= p.n_eps) break;
+                it = 0;
+                for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
+                for (int i = tid; i < N; i += blockDim.x) rowcol[i] = -1;
+                __syncthreads();
+                K = N;
+                small = small_ok && K <= ELA_SMALL_ROUND;
+                if (small) K = compact_unassigned(rowcol, N, act, s_scan);
+                continue;
+            }
+            const R eps = (R)p.eps[ph];
+#ifdef ELA_PROF
+            const long long r_t0 = clock64();
+            const int r_K = K;
+            const bool r_small = small;
+#define ELA_ROUND_END() do { if (leader && rank == 0 && tid == 0) { const unsigned long long ix = atomicAdd(&g_prof[15], 1ull); \
+                if (ix < 8192) { g_trace[ix][0] = r_K; g_trace[ix][1] = clock64() - r_t0; g_trace[ix][2] = r_small; } } } while (0)
+#else
+#define ELA_ROUND_END() do {} while (0)
+#endif
+            if (small) {
+                if (!leader) { K = 0; continue; }  // wait at the end of the epsilon
+                if (cl_pending) cluster_wait_acquire();  // everyone has read the last round's data
+                // ---- partial top-2 of my column slice for each active row,
+                //      stored straight into every CTA of the cluster (lane d -> CTA d)
+                for (int k = warp; k < K; k += nw) {
+                    const In* row = base + (int64_t)act[k] * p.stride_n;
+                    const uint4* rv = reinterpret_cast<const uint4*>(row);
+                    Top2<R> tt;
+                    top2_init(tt);
+                    for (int ch = ch0 + lane; ch < ch1; ch += 32) {
+                        const uint4 raw = ld_stream16(rv + ch);
+                        R x[W], pr[W];
+                        Elem<In>::template unpack<R>(raw, x);
+                        load_prices<R, W>(P, ch * W, pr);
+#pragma unroll
+                        for (int e = 0; e < W; ++e) top2_add(tt, sub_rn(-x[e], pr[e]), ch * W + e);
+                    }
+                    tt = top2_warp(tt);
+                    if (lane < CS) cluster.map_shared_rank(part, lane)[rank * ELA_SMALL_ROUND + k] = tt;
+                }
+                cluster_arrive_release();
+                cluster_wait_acquire();
+                // ---- each row's CS partials merged by one warp: column and bid
+                for (int k = warp; k < K; k += nw) {
+                    Top2<R> tt;
+                    top2_init(tt);
+                    if (lane < CS) tt = part[lane * ELA_SMALL_ROUND + k];
+                    tt = top2_warp(tt);
+                    if (lane == 0) {
+                        const int j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
+                        lbid[k] = add_rn(P[j1], add_rn(sub_rn(tt.v1, tt.v2), eps));
+                        lrow[k] = act[k];
+                        lcol[k] = j1;
+                    }
+                }
+                __syncthreads();
+                cluster_arrive_release();  // the partials are consumed
+                cl_pending = true;
+                rounds++;
+                rowbids += K;
+                // ---- election (identical in every CTA of the cluster)
+                if (K <= 16) {  // one warp, no CTA barrier
+                    if (warp == 0) {
+                        const bool valid = lane < K;
+                        const int j = valid ? lcol[lane] : -1;
+                        U mb = 0;
+                        for (int f = 0; f < K; ++f)
+                            if (lcol[f] == j) { const U bf = BT::to(lbid[f]); mb = bf > mb ? bf : mb; }
+                        int wrow = -1;
+                        for (int f = 0; f < K; ++f)
+                            if (lcol[f] == j && absval(sub_rn(lbid[f], BT::from(mb))) < tol) wrow = max(wrow, lrow[f]);
+                        if (valid) {
+                            int ev = -2;  // lost: bids again
+                            if (wrow == lrow[lane]) {
+                                const int prev = owner[j];
+                                if (prev >= 0) rowcol[prev] = -1;
+                                owner[j] = lrow[lane];
+                                rowcol[lrow[lane]] = j;
+                                P[j] = BT::from(mb);
+                                ev = prev;  // -1: took a free column
+                            }
+                            evict[lane] = ev;
+                        }
+                        __syncwarp();
+                    }
+                } else {
+                    for (int e = tid; e < K; e += blockDim.x) atomicMax(&maxb[lcol[e]], BT::to(lbid[e]));
+                    __syncthreads();
+                    for (int e = tid; e < K; e += blockDim.x) {
+                        const int j = lcol[e];
+                        if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[e] + 1);
+                    }
+                    __syncthreads();
+                    for (int e = tid; e < K; e += blockDim.x) {
+                        const int j = lcol[e], i = lrow[e];
+                        int ev = -2;
+                        if (win[j] == i + 1) {
+                            const int prev = owner[j];
+                            if (prev >= 0) rowcol[prev] = -1;
+                            owner[j] = i;
+                            rowcol[i] = j;
+                            P[j] = BT::from(maxb[j]);
+                            ev = prev;
+                        }
+                        evict[e] = ev;
+                    }
+                    __syncthreads();
+                    for (int e = tid; e < K; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
+                }
+                // ---- next round: losers, and rows evicted by winners, in entry order
+                if (warp == 0) {
+                    int pos = 0;
+                    for (int e0 = 0; e0 < K; e0 += 32) {
+                        const int e = e0 + lane;
+                        int r = -1;
+                        if (e < K) r = (evict[e] == -2) ? lrow[e] : evict[e];
+                        const unsigned m = __ballot_sync(0xffffffffu, r >= 0);
+                        if (r >= 0) act[pos + __popc(m & ((1u << lane) - 1))] = r;
+                        pos += __popc(m);
+                    }
+                    if (lane == 0) s_cnt = pos;
+                }
+                __syncthreads();
+                K = s_cnt;
+                ++it;
+                ELA_ROUND_END();
+                continue;
+            }
+            // ================= large round: rows split over the whole team
+            if (tid == 0) { s_cnt = 0; s_total = 0; s_extra = 0; s_fail = 0; }
+            __syncthreads();
+            for (int q = tid; q < my_rows; q += blockDim.x)
+                if (rowcol[row0 + q] < 0) act[atomicAdd(&s_cnt, 1)] = row0 + q;
+            __syncthreads();
+            const int Kl = s_cnt;
+            const unsigned int t1 = t + 1;
+            unsigned long long* myseg =
+                reinterpret_cast<unsigned long long*>(tb + (size_t)((t & 1) * ST + gi) * p.seg_bytes);
+            // one warp per row (rows are many in large rounds)
+            for (int k = warp; k < Kl; k += nw) {
+                const int i = act[k];
+                const In* row = base + (int64_t)i * p.stride_n;
+                Top2<R> tt = scan_row_fast<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                if (tt.v1 == tt.v2) tt = scan_row<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                int j1;
+                R bid;
+                finish_bid<In, R>(p, row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
+                if (lane == 0) {
+                    if (TC == 1) { const int slot = rank * rpc + k; lbid[slot] = bid; lrow[slot] = i; lcol[slot] = j1; }
+                    else put_entry<R>(myseg, k, t1, i, j1, bid);
+                }
+            }
+            int nent;
+            bool compact;  // entries at 0..nent-1 (else slots rank*rpc + k)
+            if (TC == 1) {
+                // ---- exchange through distributed shared memory
+                if (cl_pending) cluster_wait_acquire();
+                __syncthreads();
+                for (int e = tid; e < Kl * CS; e += blockDim.x) {
+                    const int k = e / CS, dst = e % CS;
+                    if (dst == rank) continue;
+                    const int slot = rank * rpc + k;
+                    cluster.map_shared_rank(lbid, dst)[slot] = lbid[slot];
+                    cluster.map_shared_rank(lrow, dst)[slot] = lrow[slot];
+                    cluster.map_shared_rank(lcol, dst)[slot] = lcol[slot];
+                }
+                if (tid < CS) cluster.map_shared_rank(cnt, tid)[rank] = Kl;
+                cluster_arrive_release();
+                cluster_wait_acquire();
+                if (tid == 0) {
+                    int acc = 0;
+                    for (int r = 0; r < CS; ++r) { s_off[r] = acc; acc += cnt[r]; }
+                    s_off[CS] = acc;
+                }
+                __syncthreads();
+                nent = s_off[CS];
+                compact = false;
+            } else {
+                // ---- exchange through tagged words in global memory (every
+                //      word carries the tag; readers re-read stale words)
+                __syncthreads();
+                if (tid == 0) st_relaxed_u64(myseg, ((unsigned long long)t1 << 32) | (unsigned int)Kl);
+                if (tid < ST) {
+                    const unsigned long long* seg =
+                        reinterpret_cast<const unsigned long long*>(tb + (size_t)((t & 1) * ST + tid) * p.seg_bytes);
+                    const unsigned long long t0 = globaltimer_ns();
+                    unsigned int spins = 0;
+                    int cntv = -1;
+                    constexpr int NW = 1 + Ex<R>::INL * Ex<R>::EW;
+                    unsigned long long w[NW];
+                    for (;;) {
+#pragma unroll
+                        for (int k = 0; k < NW; ++k) w[k] = ld_relaxed_u64(seg + k);
+                        if ((unsigned int)(w[0] >> 32) == t1) {
+                            const int cn = (int)(unsigned int)(w[0] & 0xffffffffull);
+                            bool ok = true;
+#pragma unroll
+                            for (int k = 0; k < Ex<R>::INL; ++k)
+                                if (k < cn) ok = ok && entry_tags_ok<R>(w + 1 + Ex<R>::EW * k, t1);
+                            if (ok) { cntv = cn; break; }
+                        }
+                        if ((++spins & 15u) == 0) {
+                            if (*(volatile int*)abort_flag) break;
+                            if (globaltimer_ns() - t0 > p.wait_ns) {
+                                atomicExch(abort_flag, 1);
+                                atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                                break;
+                            }
+                        }
+                    }
+                    if (cntv < 0) {
+                        s_fail = 1;
+                    } else {
+                        const int off = atomicAdd(&s_total, cntv);
+                        s_segcnt[tid] = cntv;
+                        s_off[tid] = off;
+                        if (cntv > Ex<R>::INL) s_extra = 1;
+#pragma unroll
+                        for (int k = 0; k < Ex<R>::INL; ++k)
+                            if (k < cntv) {
+                                int rr, cc;
+                                R bb;
+                                decode_entry<R>(w + 1 + Ex<R>::EW * k, rr, cc, bb);
+                                lbid[off + k] = bb; lrow[off + k] = rr; lcol[off + k] = cc;
+                            }
+                    }
+                }
+                __syncthreads();
+                if (s_fail) { if (cl_pending) cluster_wait_acquire(); cluster.sync(); return; }
+                if (s_extra && !read_extra_entries<R>(tb + (size_t)((t & 1) * ST) * p.seg_bytes, p.seg_bytes, ST,
+                                                      s_segcnt, s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag,
+                                                      p.status)) {
+                    if (cl_pending) cluster_wait_acquire();
+                    cluster.sync();
+                    return;
+                }
+                nent = s_total;
+                compact = true;
+                ++t;
+            }
+            rounds++;
+            rowbids += nent;
+            // ---- election over all bids (identical in every CTA of the team)
+            auto slot_of = [&](int e) -> int {
+                if (compact) return e;
+                int r = 0;
+                while (e >= s_off[r + 1]) ++r;
+                return r * rpc + (e - s_off[r]);
+            };
+            for (int e = tid; e < nent; e += blockDim.x) {
+                const int sl = slot_of(e);
+                atomicMax(&maxb[lcol[sl]], BT::to(lbid[sl]));
+            }
+            __syncthreads();
+            for (int e = tid; e < nent; e += blockDim.x) {
+                const int sl = slot_of(e);
+                const int j = lcol[sl];
+                if (absval(sub_rn(lbid[sl], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[sl] + 1);
+            }
+            __syncthreads();
+            for (int e = tid; e < nent; e += blockDim.x) {
+                const int sl = slot_of(e);
+                const int j = lcol[sl], i = lrow[sl];
+                if (win[j] == i + 1) {
+                    const int prev = owner[j];
+                    if (prev >= 0) rowcol[prev] = -1;
+                    owner[j] = i;
+                    rowcol[i] = j;
+                    P[j] = BT::from(maxb[j]);
+                }
+            }
+            __syncthreads();
+            for (int e = tid; e < nent; e += blockDim.x) {
+                const int sl = slot_of(e);
+                maxb[lcol[sl]] = 0;
+                win[lcol[sl]] = 0;
+            }
+            if (TC == 1) { cluster_arrive_release(); cl_pending = true; }  // the bids are consumed
+            ++it;
+            // ---- unassigned rows after the round; few -> small rounds
+            if (tid == 0) s_cnt = 0;
+            __syncthreads();
+            {
+                int mine = 0;
+                for (int i = tid; i < N; i += blockDim.x) mine += (rowcol[i] < 0);
+                if (mine) atomicAdd(&s_cnt, mine);
+            }
+            __syncthreads();
+            K = s_cnt;
+            if (small_ok && K <= ELA_SMALL_ROUND && K > 0) {
+                small = true;
+                K = compact_unassigned(rowcol, N, act, s_scan);
+            }
+            ELA_ROUND_END();
+        }
+        // ---- outputs of problem b (CTA 0 of the leader cluster)
+        if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
+        __syncthreads();
+        if (leader && rank == 0) {
+            int un = 0;
+            for (int i = tid; i < N; i += blockDim.x) {
+                p.assign_out[b * p.N + i] = rowcol[i];
+                un += (rowcol[i] < 0);
+            }
+            R* pout = reinterpret_cast<R*>(p.prices_out) + b * p.M;
+            for (int j = tid; j < M; j += blockDim.x) pout[j] = P[j];
+            if (tid == 0) s_cnt = 0;
+            __syncthreads();
+            if (un) atomicAdd(&s_cnt, un);
+            __syncthreads();
+            if (tid == 0 && p.stats_out) {
+                p.stats_out[4 * b + 0] = rounds;
+                p.stats_out[4 * b + 1] = rowbids;
+                p.stats_out[4 * b + 2] = 0;
+                p.stats_out[4 * b + 3] = s_cnt;
+            }
+        }
+        __syncthreads();
+    }
+    cluster.sync();  // no remote store may target a CTA that has exited
+}
+
 }  // namespace
 
 // ================================================================ host side
@@ -1079,6 +1645,10 @@ unsigned long long g_wait_ns = 2000000000ull;
 int g_skip_publish = 0;
 
 struct Plan {
+    int path;          // ELA_PATH_CTA / GRID / CLUSTER
+    int cs, nclusters; // cluster path: cluster size, clusters launched
+    int team;          // cluster path: clusters per problem
+    size_t team_bytes; // cluster path: workspace per team
     int S, ngroups, rpc;
     size_t smem;       // dynamic shared memory per CTA
     size_t seg_bytes;  // S > 1
@@ -1110,6 +1680,31 @@ int ctas_per_problem(int64_t B, int64_t N, int sms, int& ngroups) {
     return S < 2 ? 2 : S;
 }
 
+// Largest cluster size (16, else 8) for which at least one cluster of the
+// auction_cluster_kernel<R,R> fits with `smem` bytes per CTA; 0 if none.
+template <typename R>
+int cluster_fit(size_t smem, int& max_clusters) {
+    auto kern = auction_cluster_kernel<R, R>;
+    max_clusters = 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return 0;
+    for (int cs = 16; cs >= 8; cs /= 2) {
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = cs; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(cs); cfg.blockDim = dim3(ELA_THREADS_MULTI); cfg.dynamicSmemBytes = smem;
+        cfg.attrs = attr; cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) == cudaSuccess && n > 0) {
+            max_clusters = n;
+            return cs;
+        }
+        cudaGetLastError();  // clear a refusal of this cluster size
+    }
+    return 0;
+}
+
 template <typename R>
 int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_max, Plan& pl) {
     const size_t one_smem = k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32).total;
@@ -1120,14 +1715,56 @@ int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_
     const size_t multi_smem = k_layout<R>(N, M, rpc, ELA_THREADS_MULTI / 32).total;
     const bool multi_fits = multi_smem <= smem_max && N < (1 << 24) && M < (1 << 24) && N >= 2;
 
+    // cluster plan (sizes only; the largest cluster size the device accepts)
+    int cs = 0, max_clusters = 0;
+    size_t cl_smem = 0;
+    bool cl_fits = false;
+    const bool no_cluster = (path == -1);
+    if (no_cluster) path = ELA_PATH_AUTO;
+    if (!no_cluster && M >= ELA_SMALL_M && N >= 2 && N < (1 << 24) &&
+        (path == ELA_PATH_AUTO || path == ELA_PATH_CLUSTER)) {
+        cl_smem = c_layout<R>(N, M, 16).total;
+        if (cl_smem <= smem_max) cs = cluster_fit<R>(cl_smem, max_clusters);
+        if (cs == 8) {
+            cl_smem = c_layout<R>(N, M, 8).total;
+            if (cl_smem > smem_max) cs = 0;
+        }
+        cl_fits = cs > 0;
+    }
+
     int chosen = path;
     if (path == ELA_PATH_AUTO) {
         if (one_fits && (N <= 512 || B >= sms)) chosen = ELA_PATH_CTA;
+        else if (cl_fits) chosen = ELA_PATH_CLUSTER;
         else if (multi_fits) chosen = ELA_PATH_GRID;
         else if (one_fits) chosen = ELA_PATH_CTA;
         else return ELA_ERR_UNSUPPORTED;
     }
-    if (chosen == ELA_PATH_CTA) {
+    pl.path = chosen;
+    if (chosen == ELA_PATH_CLUSTER) {
+        if (!cl_fits) return ELA_ERR_UNSUPPORTED;
+        pl.cs = cs;
+        // few problems: a team of clusters per problem shares its large rounds
+        int team = 1, nteams = max_clusters;
+        if (B < max_clusters) { nteams = (int)B; team = max_clusters / (int)B; }
+        if (const char* env = getenv("ELA_CLUSTERS_PER_PROBLEM")) {  // tuning knob
+            const int v = atoi(env);
+            if (v >= 1 && v < team) team = v;
+        }
+        while (team * cs > ELA_MAX_S) --team;
+        pl.team = team;
+        pl.ngroups = nteams;
+        pl.nclusters = nteams * team;
+        pl.S = team * cs;
+        pl.rpc = (int)((N + pl.S - 1) / pl.S);
+        pl.smem = cl_smem;
+        pl.seg_bytes = align_up(8 + 8 * (size_t)Ex<R>::EW * pl.rpc, 128);
+        pl.team_bytes = (team > 1) ? align_up(2 * (size_t)pl.S * pl.seg_bytes + align_up(sizeof(R) * (size_t)M, 256) + 256, 256) : 0;
+        pl.ws_bytes = ELA_WS_HEADER + (size_t)nteams * pl.team_bytes;
+        if (getenv("ELA_DEBUG_PLAN"))
+            fprintf(stderr, "ela plan: cluster cs=%d max_clusters=%d team=%d teams=%d smem=%zu\n", cs, max_clusters,
+                    team, nteams, cl_smem);
+    } else if (chosen == ELA_PATH_CTA) {
         if (!one_fits) return ELA_ERR_UNSUPPORTED;
         pl.S = 1; pl.ngroups = 0; pl.rpc = (int)N;
         pl.smem = one_smem;
@@ -1156,21 +1793,45 @@ int device_limits(int& sms, size_t& smem_max) {
     return ELA_OK;
 }
 
-int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl) {
+int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bool allow_cluster = true) {
     if (elem_size(dtype) == 0 || B < 0 || N < 0 || M < 0) return ELA_ERR_ARGUMENT;
-    if (path < ELA_PATH_AUTO || path > ELA_PATH_GRID) return ELA_ERR_ARGUMENT;
+    if (path < ELA_PATH_AUTO || path > ELA_PATH_CLUSTER) return ELA_ERR_ARGUMENT;
     if (N > 0 && M < 2) return ELA_ERR_ARGUMENT;
     if (N >= (1ll << 30) || M >= (1ll << 30)) return ELA_ERR_UNSUPPORTED;
     int sms = 0;
     size_t smem_max = 0;
     const int rc = device_limits(sms, smem_max);
     if (rc != ELA_OK) return rc;
-    return dtype == ELA_DTYPE_F64 ? make_plan_t<double>(B, N, M, path, sms, smem_max, pl)
-                                  : make_plan_t<float>(B, N, M, path, sms, smem_max, pl);
+    if (!allow_cluster && path == ELA_PATH_CLUSTER) return ELA_ERR_UNSUPPORTED;
+    const int ask = (!allow_cluster && path == ELA_PATH_AUTO) ? -1 : path;
+    return dtype == ELA_DTYPE_F64 ? make_plan_t<double>(B, N, M, ask, sms, smem_max, pl)
+                                  : make_plan_t<float>(B, N, M, ask, sms, smem_max, pl);
 }
 
 template <typename In, typename R>
 int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
+    if (pl.path == ELA_PATH_CLUSTER) {
+        if (!p.vec_ok) return ELA_ERR_UNSUPPORTED;  // rows must allow 16-byte loads
+        auto kern = auction_cluster_kernel<In, R>;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
+            return ELA_ERR_CUDA;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+            return ELA_ERR_CUDA;
+        cudaLaunchConfig_t cfg = {};
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = pl.cs; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+        cfg.gridDim = dim3(pl.cs * pl.nclusters);
+        cfg.blockDim = dim3(ELA_THREADS_MULTI);
+        cfg.dynamicSmemBytes = pl.smem;
+        cfg.stream = stream;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        // The launch never exceeds the clusters that fit at once (occupancy
+        // query), so the clusters of a team, which wait on one another, are
+        // co-resident; every such wait is also bounded.
+        return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
+    }
     if (pl.S == 1) {
         auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, ELA_UNROLL_ONE>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
@@ -1299,9 +1960,14 @@ const char* ela_status_string(int status) {
 }
 
 size_t ela_auction_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t M, int path) {
-    Plan pl;
+    Plan pl = {};
     if (make_plan(dtype, B, N, M, path, pl) != ELA_OK) return 0;
-    return pl.ws_bytes;
+    size_t ws = pl.ws_bytes;
+    // AUTO may fall back from the cluster path for rows without 16-byte alignment
+    Plan alt = {};
+    if (path == ELA_PATH_AUTO && make_plan(dtype, B, N, M, path, alt, false) == ELA_OK && alt.ws_bytes > ws)
+        ws = alt.ws_bytes;
+    return ws;
 }
 
 void ela_auction_set_wait_limit_ns(uint64_t ns) { g_wait_ns = ns ? ns : 1; }
@@ -1322,8 +1988,8 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
     rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, assign_out,
                      prices_out, stats_out, p);
     if (rc != ELA_OK) return rc;
-    Plan pl;
-    rc = make_plan(dtype, B, N, M, path, pl);
+    Plan pl = {};
+    rc = make_plan(dtype, B, N, M, path, pl, p.vec_ok != 0);
     if (rc != ELA_OK) return rc;
     if (workspace_bytes < pl.ws_bytes) return ELA_ERR_ARGUMENT;
     unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
@@ -1333,6 +1999,8 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
     p.S = pl.S;
     p.ngroups = pl.ngroups;
     p.rows_per_cta = pl.rpc;
+    p.team = pl.team;
+    p.team_bytes = pl.team_bytes;
     if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
@@ -1354,8 +2022,8 @@ int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N,
     rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, assign_out,
                      prices_out, stats_out, p);
     if (rc != ELA_OK) return rc;
-    Plan pl;
-    rc = make_plan(dtype, B, N, M, path, pl);
+    Plan pl = {};
+    rc = make_plan(dtype, B, N, M, path, pl, p.vec_ok != 0);
     if (rc != ELA_OK) return rc;
     if (pl.ws_bytes > (size_t)ELA_NOALLOC_SCRATCH_BYTES) return ELA_ERR_UNSUPPORTED;
     void* scratch = nullptr;
@@ -1368,6 +2036,8 @@ int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N,
     p.S = pl.S;
     p.ngroups = pl.ngroups;
     p.rows_per_cta = pl.rpc;
+    p.team = pl.team;
+    p.team_bytes = pl.team_bytes;
     // The array keeps the previous call's contents: clear the part this solve
     // uses (abort flag, status word, exchange tags must start at zero).
     if (cudaMemsetAsync(scratch, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;

@@ -41,8 +41,12 @@ enum {
 /* Element type of the cost matrix. */
 enum { ELA_DTYPE_F32 = 0, ELA_DTYPE_F16 = 1, ELA_DTYPE_BF16 = 2, ELA_DTYPE_F64 = 3 };
 
-/* Kernel choice.  AUTO picks by batch and problem size. */
-enum { ELA_PATH_AUTO = 0, ELA_PATH_CTA = 1, ELA_PATH_GRID = 2 };
+/* Kernel choice.  AUTO picks by batch and problem size.
+ *   CTA      one CTA per problem (batches of small problems)
+ *   GRID     several co-resident CTAs per problem, bids exchanged through global memory
+ *   CLUSTER  one thread-block cluster per problem, bids exchanged through
+ *            distributed shared memory (few large problems; needs M >= 128) */
+enum { ELA_PATH_AUTO = 0, ELA_PATH_CTA = 1, ELA_PATH_GRID = 2, ELA_PATH_CLUSTER = 3 };
 
 /* Library ABI version (major*100 + minor). */
 int ela_auction_version(void);

@@ -11,7 +11,7 @@ from make_golden_io import load_golden
 
 pytestmark = pytest.mark.gpu
 
-PATHS = {"auto": ela.PATH_AUTO, "cta": ela.PATH_CTA, "grid": ela.PATH_GRID}
+PATHS = {"auto": ela.PATH_AUTO, "cta": ela.PATH_CTA, "grid": ela.PATH_GRID, "cluster": ela.PATH_CLUSTER}
 BIG = {"cfg2_fixed", "cfg2_escale", "cfg2_maxiter10", "cfg3_f16", "cfg3_bf16"}
 
 
@@ -39,7 +39,7 @@ def test_golden_bit_exact(name, path):
     assert torch.equal(st[:, 3], (a == -1).sum(1))
 
 
-@pytest.mark.parametrize("path", ["cta", "grid"])
+@pytest.mark.parametrize("path", ["cta", "grid", "cluster"])
 @pytest.mark.parametrize("seed", range(4))
 def test_random_vs_oracle(seed, path, oracle_mod):
     g = torch.Generator().manual_seed(1000 + seed)
@@ -68,7 +68,7 @@ def test_cfg4_full_batch_vs_oracle(oracle_mod):
 @pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float64])
 def test_dtypes_vs_oracle(dtype, oracle_mod):
     cost = ela.workloads.uniform(2, 256, 256, seed=77, dtype=dtype)
-    for path in (ela.PATH_CTA, ela.PATH_GRID):
+    for path in (ela.PATH_CTA, ela.PATH_GRID, ela.PATH_CLUSTER):
         a, p, _ = gpu_solve(cost, 1e-3, 1000, path)
         ao, po, _ = oracle_mod.solve(cost, 1e-3, 1000)
         assert torch.equal(a, ao) and torch.equal(p, po)
