@@ -1155,7 +1155,7 @@ __host__ __device__ inline CLayout c_layout(int64_t N, int64_t M, int CS) {
     L.lbid = o;   o = align_up(o + sizeof(R) * nlist, 16);
     L.lrow = o;   o = align_up(o + 4 * nlist, 16);
     L.lcol = o;   o = align_up(o + 4 * nlist, 16);
-    L.part = o;   o = align_up(o + sizeof(Top2<R>) * (size_t)CS * ELA_SMALL_ROUND, 16);
+    L.part = o;   o = align_up(o + 2 * sizeof(Top2<R>) * (size_t)CS * ELA_SMALL_ROUND, 16);  // by round parity
     L.cnt = o;    o = align_up(o + 4 * (size_t)CS, 16);
     L.evict = o;  o = align_up(o + 4 * (size_t)ELA_SMALL_ROUND, 16);
     L.total = o;
@@ -1167,6 +1167,40 @@ __device__ __forceinline__ void cluster_arrive_release() {
 }
 __device__ __forceinline__ void cluster_wait_acquire() {
     asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+
+// ---- asynchronous stores into another CTA's shared memory, completed on
+// that CTA's mbarrier (transaction bytes), and the local mbarrier wait.
+__device__ __forceinline__ unsigned int smem_addr(const void* ptr) {
+    return (unsigned int)__cvta_generic_to_shared(ptr);
+}
+__device__ __forceinline__ unsigned int cluster_map(unsigned int addr, int rank) {
+    unsigned int r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_async_16(unsigned int raddr, uint4 v, unsigned int rmbar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+                 ::"r"(raddr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w), "r"(rmbar) : "memory");
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* mb, unsigned int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(mb)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* mb, unsigned int bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(mb)), "r"(bytes) : "memory");
+}
+// Bounded wait for phase `parity` of a local mbarrier; false on timeout.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int parity, unsigned long long limit_ns) {
+    const unsigned int a = smem_addr(mb);
+    const unsigned long long t0 = globaltimer_ns();
+    for (;;) {
+        unsigned int done;
+        asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                     : "=r"(done) : "r"(a), "r"(parity) : "memory");
+        if (done) return true;
+        if (globaltimer_ns() - t0 > limit_ns) return false;
+    }
 }
 
 // Block-wide ordered compaction of the rows with rowcol < 0 into act[];
@@ -1223,6 +1257,9 @@ auction_cluster_kernel(const Params p) {
     __shared__ int s_off[ELA_MAX_S + 1];
     __shared__ int s_segcnt[ELA_MAX_S];
     __shared__ int s_exoff[ELA_MAX_S + 1];
+    __shared__ __align__(8) unsigned long long s_mbar[2];  // small-round partials, by round parity
+    // fp32 partials are 16 bytes: one asynchronous store per destination CTA
+    constexpr bool ASYNC = (sizeof(Top2<R>) == 16);
 
     cg::cluster_group cluster = cg::this_cluster();
     const int CS = (int)cluster.num_blocks();
@@ -1266,6 +1303,12 @@ auction_cluster_kernel(const Params p) {
     bool cl_pending = false;      // a "consumed" arrival on the cluster barrier awaits its wait
     unsigned int t = 0;           // global-exchange round tag (large rounds, TC > 1)
     unsigned int seq = 0;         // epsilons the leader has published (TC > 1)
+    unsigned int sr = 0;          // small rounds run by this cluster (parity of the partial buffers)
+    if (tid == 0) {
+        mbar_init(&s_mbar[0], 1);
+        mbar_init(&s_mbar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
     cluster.sync();               // every CTA of the cluster runs before any remote store
 
     for (int64_t b = team; b < p.B; b += p.ngroups) {
@@ -1280,6 +1323,11 @@ auction_cluster_kernel(const Params p) {
         if (small) K = compact_unassigned(rowcol, N, act, s_scan);
         while (ph < p.n_eps) {
             if (it == p.max_iter || K == 0) {  // this epsilon is done
+                if (small) {  // the cluster's next stores into its CTAs' bid lists wait for everyone
+                    if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
+                    cluster_arrive_release();
+                    cluster_wait_acquire();
+                }
                 if (small && TC > 1) {
                     // the leader publishes its prices; the other clusters wait for them
                     ++seq;
@@ -1335,7 +1383,11 @@ auction_cluster_kernel(const Params p) {
 #endif
             if (small) {
                 if (!leader) { K = 0; continue; }  // wait at the end of the epsilon
-                if (cl_pending) cluster_wait_acquire();  // everyone has read the last round's data
+                if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }  // last round's data read everywhere
+                const int bp = ASYNC ? (int)(sr & 1) : 0;
+                Top2<R>* pb = part + (size_t)bp * CS * ELA_SMALL_ROUND;
+                if (ASYNC && tid == 0)
+                    mbar_expect_tx(&s_mbar[bp], (unsigned int)(K * (CS - 1) * sizeof(Top2<R>)));
                 // ---- partial top-2 of my column slice for each active row,
                 //      stored straight into every CTA of the cluster (lane d -> CTA d)
                 for (int k = warp; k < K; k += nw) {
@@ -1352,15 +1404,34 @@ auction_cluster_kernel(const Params p) {
                         for (int e = 0; e < W; ++e) top2_add(tt, sub_rn(-x[e], pr[e]), ch * W + e);
                     }
                     tt = top2_warp(tt);
-                    if (lane < CS) cluster.map_shared_rank(part, lane)[rank * ELA_SMALL_ROUND + k] = tt;
+                    if (ASYNC) {
+                        Top2<R>* slot = pb + rank * ELA_SMALL_ROUND + k;
+                        if (lane == rank) *slot = tt;
+                        else if (lane < CS)
+                            st_async_16(cluster_map(smem_addr(slot), lane), *reinterpret_cast<const uint4*>(&tt),
+                                        cluster_map(smem_addr(&s_mbar[bp]), lane));
+                    } else if (lane < CS) {
+                        cluster.map_shared_rank(pb, lane)[rank * ELA_SMALL_ROUND + k] = tt;
+                    }
                 }
-                cluster_arrive_release();
-                cluster_wait_acquire();
+                if (ASYNC) {
+                    if (tid == 0) s_fail = !mbar_wait(&s_mbar[bp], (sr >> 1) & 1u, p.wait_ns);
+                    __syncthreads();
+                    if (s_fail) {
+                        atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                        cluster.sync();
+                        return;
+                    }
+                    ++sr;
+                } else {
+                    cluster_arrive_release();
+                    cluster_wait_acquire();
+                }
                 // ---- each row's CS partials merged by one warp: column and bid
                 for (int k = warp; k < K; k += nw) {
                     Top2<R> tt;
                     top2_init(tt);
-                    if (lane < CS) tt = part[lane * ELA_SMALL_ROUND + k];
+                    if (lane < CS) tt = pb[lane * ELA_SMALL_ROUND + k];
                     tt = top2_warp(tt);
                     if (lane == 0) {
                         const int j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
@@ -1370,8 +1441,7 @@ auction_cluster_kernel(const Params p) {
                     }
                 }
                 __syncthreads();
-                cluster_arrive_release();  // the partials are consumed
-                cl_pending = true;
+                if (!ASYNC) { cluster_arrive_release(); cl_pending = true; }  // the partials are consumed
                 rounds++;
                 rowbids += K;
                 // ---- election (identical in every CTA of the cluster)
@@ -1609,8 +1679,11 @@ auction_cluster_kernel(const Params p) {
             }
             ELA_ROUND_END();
         }
-        // ---- outputs of problem b (CTA 0 of the leader cluster)
+        // ---- outputs of problem b (CTA 0 of the leader cluster); every CTA of
+        //      the cluster is done with this problem's shared data
         if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
+        cluster_arrive_release();
+        cluster_wait_acquire();
         __syncthreads();
         if (leader && rank == 0) {
             int un = 0;
