@@ -1383,6 +1383,7 @@ auction_cluster_kernel(const Params p) {
 #endif
             if (small) {
                 if (!leader) { K = 0; continue; }  // wait at the end of the epsilon
+                PROF_MARK(q0);
                 if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }  // last round's data read everywhere
                 const int bp = ASYNC ? (int)(sr & 1) : 0;
                 Top2<R>* pb = part + (size_t)bp * CS * ELA_SMALL_ROUND;
@@ -1397,13 +1398,29 @@ auction_cluster_kernel(const Params p) {
                     top2_init(tt);
                     for (int ch = ch0 + lane; ch < ch1; ch += 32) {
                         const uint4 raw = ld_stream16(rv + ch);
-                        R x[W], pr[W];
+                        R x[W], pr[W], v[W];
                         Elem<In>::template unpack<R>(raw, x);
                         load_prices<R, W>(P, ch * W, pr);
 #pragma unroll
-                        for (int e = 0; e < W; ++e) top2_add(tt, sub_rn(-x[e], pr[e]), ch * W + e);
+                        for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
+                        R mx, sd;
+                        int ix;
+                        chunk_top2<R, W>(v, mx, sd, ix);
+                        lane_merge(tt, mx, sd, ch * W + ix);
                     }
-                    tt = top2_warp(tt);
+                    tt = top2_warp_fast(tt);
+                    if (tt.p1 >= 0 && tt.v1 == tt.v2) {  // tied maximum in the slice: exact columns
+                        top2_init(tt);
+                        for (int ch = ch0 + lane; ch < ch1; ch += 32) {
+                            const uint4 raw = ld_stream16(rv + ch);
+                            R x[W], pr[W];
+                            Elem<In>::template unpack<R>(raw, x);
+                            load_prices<R, W>(P, ch * W, pr);
+#pragma unroll
+                            for (int e = 0; e < W; ++e) top2_add(tt, sub_rn(-x[e], pr[e]), ch * W + e);
+                        }
+                        tt = top2_warp(tt);
+                    }
                     if (ASYNC) {
                         Top2<R>* slot = pb + rank * ELA_SMALL_ROUND + k;
                         if (lane == rank) *slot = tt;
@@ -1414,6 +1431,7 @@ auction_cluster_kernel(const Params p) {
                         cluster.map_shared_rank(pb, lane)[rank * ELA_SMALL_ROUND + k] = tt;
                     }
                 }
+                PROF_MARK(q1);
                 if (ASYNC) {
                     if (tid == 0) s_fail = !mbar_wait(&s_mbar[bp], (sr >> 1) & 1u, p.wait_ns);
                     __syncthreads();
@@ -1440,7 +1458,9 @@ auction_cluster_kernel(const Params p) {
                         lcol[k] = j1;
                     }
                 }
+                PROF_MARK(q2);
                 __syncthreads();
+                PROF_MARK(q3);
                 if (!ASYNC) { cluster_arrive_release(); cl_pending = true; }  // the partials are consumed
                 rounds++;
                 rowbids += K;
@@ -1507,6 +1527,14 @@ auction_cluster_kernel(const Params p) {
                     if (lane == 0) s_cnt = pos;
                 }
                 __syncthreads();
+                PROF_MARK(q4);
+#ifdef ELA_PROF
+                if (leader && rank == 0 && tid == 0) {
+                    atomicAdd(&g_prof[0], (unsigned long long)(q1 - q0)); atomicAdd(&g_prof[1], (unsigned long long)(q2 - q1));
+                    atomicAdd(&g_prof[2], (unsigned long long)(q3 - q2)); atomicAdd(&g_prof[3], (unsigned long long)(q4 - q3));
+                    atomicAdd(&g_prof[4], 1ull); atomicAdd(&g_prof[5], (unsigned long long)(q0 - r_t0));
+                }
+#endif
                 K = s_cnt;
                 ++it;
                 ELA_ROUND_END();
