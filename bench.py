@@ -114,7 +114,7 @@ def traffic_per_launch():
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
     try:
         with open(os.path.join(ROOT, "profiles", "roofline_inputs.json")) as f:
-            return json.load(f).get("grid_kernel_cfg2_dram_bytes_per_launch")
+            return json.load(f).get("cfg2_solve_kernel_dram_bytes_per_launch")
     except Exception:
         return None
 
