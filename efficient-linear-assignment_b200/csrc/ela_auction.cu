@@ -802,6 +802,7 @@ auction_kernel(const Params p) {
     typedef typename BT::U U;
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_nact, s_total, s_extra, s_fail;
+    __shared__ int s_ties, s_exact;  // rows whose maximum tied; scan exactly first when many do
     __shared__ int s_cnt[MULTI ? ELA_MAX_S : 1], s_off[MULTI ? ELA_MAX_S : 1];
     __shared__ int s_exoff[MULTI ? ELA_MAX_S + 1 : 1];
     __shared__ int s_unassigned;
@@ -830,6 +831,7 @@ auction_kernel(const Params p) {
     int* abort_flag = reinterpret_cast<int*>(p.ws);
     unsigned char* gbase = p.ws + ELA_WS_HEADER + (size_t)g * 2 * S * p.seg_bytes;
 
+    if (tid == 0) { s_ties = 0; s_exact = 0; }
     const int nprob_step = MULTI ? p.ngroups : gridDim.x;
     unsigned int t = 0;  // round counter, identical in all CTAs of a group
     bool first_publish = true;
@@ -906,7 +908,9 @@ auction_kernel(const Params p) {
                         if (warp == 0 && lane == 0 && t < 8192) { g_trace[t][11] = a00 - pt1; g_trace[t][7] = d[0]; g_trace[t][4] = d[1]; }
                     } else
 #endif
-                    if (has) tt = scan_row_fast<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                    const bool exact_first = (wpr == 1) && s_exact;  // tie-heavy rows: one exact pass
+                    if (has) tt = exact_first ? scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1)
+                                              : scan_row_fast<In, R, UNROLL>(p, row, P, lane, sub, wpr);
 #ifdef ELA_PROF
                     if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][8], (unsigned long long)(clock64() - pt1));
 #endif
@@ -937,9 +941,10 @@ auction_kernel(const Params p) {
                                 tt = top2_warp(o);
                             }
                         }
-                    } else if (exact_ok && has && tt.v1 == tt.v2) {
+                    } else if (exact_ok && has && tt.v1 == tt.v2 && !exact_first) {
                         tt = scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1);
                     }
+                    if (has && sub == 0 && lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
 #ifdef ELA_PROF
                     if (has && sub == 0 && lane == 0 && t < 8192) atomicMax(&g_trace[t][9], (unsigned long long)(clock64() - pt1));
 #endif
@@ -960,6 +965,7 @@ auction_kernel(const Params p) {
                 }
             }
             __syncthreads();
+            if (tid == 0) { s_exact = (K > 0) ? (s_ties * 4 > K) : s_exact; s_ties = 0; }
             PROF_MARK(pt2);
             // ---- gather the round's bids of the whole problem
             int ntot;
@@ -1254,6 +1260,7 @@ auction_cluster_kernel(const Params p) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int s_scan[32];
     __shared__ int s_cnt, s_total, s_extra, s_fail;
+    __shared__ int s_ties, s_exact;  // rows whose maximum tied; scan exactly first when many do
     __shared__ int s_off[ELA_MAX_S + 1];
     __shared__ int s_segcnt[ELA_MAX_S];
     __shared__ int s_exoff[ELA_MAX_S + 1];
@@ -1305,6 +1312,8 @@ auction_cluster_kernel(const Params p) {
     unsigned int seq = 0;         // epsilons the leader has published (TC > 1)
     unsigned int sr = 0;          // small rounds run by this cluster (parity of the partial buffers)
     if (tid == 0) {
+        s_ties = 0;
+        s_exact = 0;
         mbar_init(&s_mbar[0], 1);
         mbar_init(&s_mbar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1554,8 +1563,14 @@ auction_cluster_kernel(const Params p) {
             for (int k = warp; k < Kl; k += nw) {
                 const int i = act[k];
                 const In* row = base + (int64_t)i * p.stride_n;
-                Top2<R> tt = scan_row_fast<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
-                if (tt.v1 == tt.v2) tt = scan_row<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                Top2<R> tt;
+                if (s_exact) {  // tie-heavy rows: one exact pass
+                    tt = scan_row<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                } else {
+                    tt = scan_row_fast<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                    if (tt.v1 == tt.v2) tt = scan_row<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                }
+                if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                 int j1;
                 R bid;
                 finish_bid<In, R>(p, row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
@@ -1564,6 +1579,8 @@ auction_cluster_kernel(const Params p) {
                     else put_entry<R>(myseg, k, t1, i, j1, bid);
                 }
             }
+            __syncthreads();
+            if (tid == 0) { s_exact = (Kl > 0) ? (s_ties * 4 > Kl) : s_exact; s_ties = 0; }
             int nent;
             bool compact;  // entries at 0..nent-1 (else slots rank*rpc + k)
             if (TC == 1) {
