@@ -697,9 +697,9 @@ __device__ __forceinline__ bool get_entry(const unsigned long long* seg, int k, 
 // spread over the whole CTA (one L2 latency, not one per segment).  cnt/off:
 // per-segment counts and list offsets; exoff: S+1 ints of shared scratch.
 // Returns false if an entry never showed up (status and abort flag are set).
-template <typename R>
+template <typename R, typename IX = int>
 __device__ bool read_extra_entries(const unsigned char* segbase, size_t seg_bytes, int S, const int* cnt,
-                                   const int* off, int* exoff, unsigned int t1, R* lbid, int* lrow, int* lcol,
+                                   const int* off, int* exoff, unsigned int t1, R* lbid, IX* lrow, IX* lcol,
                                    int* abort_flag, int32_t* status) {
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid < 32) {  // exclusive prefix of the extra counts, one warp
@@ -738,7 +738,7 @@ __device__ bool read_extra_entries(const unsigned char* segbase, size_t seg_byte
                 break;
             }
         }
-        lbid[off[lo] + k] = bb; lrow[off[lo] + k] = rr; lcol[off[lo] + k] = cc;
+        lbid[off[lo] + k] = bb; lrow[off[lo] + k] = (IX)rr; lcol[off[lo] + k] = (IX)cc;
     }
     return __syncthreads_and(ok) != 0;
 }
@@ -1144,23 +1144,24 @@ auction_kernel(const Params p) {
 #define ELA_SMALL_ROUND 64
 
 struct CLayout {
-    size_t P, maxb, win, owner, rowcol, act, lbid, lrow, lcol, part, cnt, evict, total;
+    size_t P, win, owner, rowcol, act, lbid, lrow, lcol, part, cnt, evict, total;
 };
-template <typename R>
+// IX: index type of rows and columns in shared memory (16-bit when N and M
+// are below 32768, which halves the footprint of the replicated state).
+template <typename R, typename IX>
 __host__ __device__ inline CLayout c_layout(int64_t N, int64_t M, int CS) {
     CLayout L;
     const int rpc = (int)((N + CS - 1) / CS);
-    const size_t nlist = (size_t)rpc * CS;  // slot rank*rpc + k
+    const size_t nlist = (size_t)rpc * CS;  // bid list: slot rank*rpc + k (DSMEM) or 0..K-1
     size_t o = 0;
-    L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);
-    L.maxb = o;   o = align_up(o + sizeof(R) * (size_t)M, 16);
-    L.win = o;    o = align_up(o + 4 * (size_t)M, 16);
-    L.owner = o;  o = align_up(o + 4 * (size_t)M, 16);
-    L.rowcol = o; o = align_up(o + 4 * (size_t)N, 16);
-    L.act = o;    o = align_up(o + 4 * (size_t)N, 16);
+    L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);   // prices (the round's max bid lands here)
+    L.win = o;    o = align_up(o + 4 * (size_t)M, 16);           // elected row + 1 per column
+    L.owner = o;  o = align_up(o + sizeof(IX) * (size_t)M, 16);  // row owning each column, -1
+    L.rowcol = o; o = align_up(o + sizeof(IX) * (size_t)N, 16);  // column of each row, -1
+    L.act = o;    o = align_up(o + sizeof(IX) * (size_t)N, 16);  // rows bidding this round, ascending
     L.lbid = o;   o = align_up(o + sizeof(R) * nlist, 16);
-    L.lrow = o;   o = align_up(o + 4 * nlist, 16);
-    L.lcol = o;   o = align_up(o + 4 * nlist, 16);
+    L.lrow = o;   o = align_up(o + sizeof(IX) * nlist, 16);
+    L.lcol = o;   o = align_up(o + sizeof(IX) * nlist, 16);
     L.part = o;   o = align_up(o + 2 * sizeof(Top2<R>) * (size_t)CS * ELA_SMALL_ROUND, 16);  // by round parity
     L.cnt = o;    o = align_up(o + 4 * (size_t)CS, 16);
     L.evict = o;  o = align_up(o + 4 * (size_t)ELA_SMALL_ROUND, 16);
@@ -1211,7 +1212,8 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int p
 
 // Block-wide ordered compaction of the rows with rowcol < 0 into act[];
 // returns the count (all threads).  Deterministic: ascending row order.
-__device__ int compact_unassigned(const int* rowcol, int N, int* act, int* s_scan) {
+template <typename IX>
+__device__ int compact_unassigned(const IX* rowcol, int N, IX* act, int* s_scan) {
     const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
     const int chunk = (N + nt - 1) / nt;
     const int r0 = tid * chunk, r1 = min(N, r0 + chunk);
@@ -1238,7 +1240,7 @@ __device__ int compact_unassigned(const int* rowcol, int N, int* act, int* s_sca
     __syncthreads();
     int pos = x - mine + (warp > 0 ? s_scan[warp - 1] : 0);
     for (int i = r0; i < r1; ++i)
-        if (rowcol[i] < 0) act[pos++] = i;
+        if (rowcol[i] < 0) act[pos++] = (IX)i;
     const int total = s_scan[nw - 1];
     __syncthreads();
     return total;
@@ -1251,7 +1253,7 @@ __device__ int compact_unassigned(const int* rowcol, int N, int* act, int* s_sca
 // run in the team's first (leader) cluster only; the other clusters wait for
 // the end of the epsilon and then reload the prices the leader publishes.
 // Per-team workspace: [2 x ST exchange segments][prices M][flag word].
-template <typename In, typename R>
+template <typename In, typename R, typename IX>
 __global__ void __launch_bounds__(ELA_THREADS_MULTI, 1)
 auction_cluster_kernel(const Params p) {
     namespace cg = cooperative_groups;
@@ -1281,18 +1283,17 @@ auction_cluster_kernel(const Params p) {
     const int N = (int)p.N, M = (int)p.M;
     constexpr int W = Elem<In>::W;
     const int nchunks = M / W;
-    const int rpc = (N + ST - 1) / ST;        // large rounds: rows per CTA
-    const int row0 = gi * rpc, my_rows = max(0, min(rpc, N - row0));
-    const CLayout L = c_layout<R>(N, M, CS);
+    const int rpc = (N + CS - 1) / CS;        // DSMEM bid-list slots per CTA
+    const CLayout L = c_layout<R, IX>(N, M, CS);
     R* P = reinterpret_cast<R*>(smem + L.P);
-    U* maxb = reinterpret_cast<U*>(smem + L.maxb);
+    U* Pbits = reinterpret_cast<U*>(smem + L.P);
     int* win = reinterpret_cast<int*>(smem + L.win);
-    int* owner = reinterpret_cast<int*>(smem + L.owner);
-    int* rowcol = reinterpret_cast<int*>(smem + L.rowcol);
-    int* act = reinterpret_cast<int*>(smem + L.act);
+    IX* owner = reinterpret_cast<IX*>(smem + L.owner);
+    IX* rowcol = reinterpret_cast<IX*>(smem + L.rowcol);
+    IX* act = reinterpret_cast<IX*>(smem + L.act);
     R* lbid = reinterpret_cast<R*>(smem + L.lbid);
-    int* lrow = reinterpret_cast<int*>(smem + L.lrow);
-    int* lcol = reinterpret_cast<int*>(smem + L.lcol);
+    IX* lrow = reinterpret_cast<IX*>(smem + L.lrow);
+    IX* lcol = reinterpret_cast<IX*>(smem + L.lcol);
     Top2<R>* part = reinterpret_cast<Top2<R>*>(smem + L.part);
     int* cnt = reinterpret_cast<int*>(smem + L.cnt);
     int* evict = reinterpret_cast<int*>(smem + L.evict);
@@ -1322,14 +1323,13 @@ auction_cluster_kernel(const Params p) {
 
     for (int64_t b = team; b < p.B; b += p.ngroups) {
         const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
-        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; maxb[j] = 0; win[j] = 0; owner[j] = -1; }
-        for (int i = tid; i < N; i += blockDim.x) rowcol[i] = -1;
+        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; win[j] = 0; owner[j] = (IX)-1; }
+        for (int i = tid; i < N; i += blockDim.x) rowcol[i] = (IX)-1;
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
         __syncthreads();
-        int K = N;  // rows that bid this round (every CTA of the team agrees)
+        int K = compact_unassigned(rowcol, N, act, s_scan);  // rows that bid this round, ascending
         bool small = small_ok && K <= ELA_SMALL_ROUND;
-        if (small) K = compact_unassigned(rowcol, N, act, s_scan);
         while (ph < p.n_eps) {
             if (it == p.max_iter || K == 0) {  // this epsilon is done
                 if (small) {  // the cluster's next stores into its CTAs' bid lists wait for everyone
@@ -1372,27 +1372,16 @@ auction_cluster_kernel(const Params p) {
                 }
                 if (++ph >= p.n_eps) break;
                 it = 0;
-                for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
-                for (int i = tid; i < N; i += blockDim.x) rowcol[i] = -1;
+                for (int j = tid; j < M; j += blockDim.x) owner[j] = (IX)-1;
+                for (int i = tid; i < N; i += blockDim.x) rowcol[i] = (IX)-1;
                 __syncthreads();
-                K = N;
+                K = compact_unassigned(rowcol, N, act, s_scan);
                 small = small_ok && K <= ELA_SMALL_ROUND;
-                if (small) K = compact_unassigned(rowcol, N, act, s_scan);
                 continue;
             }
             const R eps = (R)p.eps[ph];
-#ifdef ELA_PROF
-            const long long r_t0 = clock64();
-            const int r_K = K;
-            const bool r_small = small;
-#define ELA_ROUND_END() do { if (leader && rank == 0 && tid == 0) { const unsigned long long ix = atomicAdd(&g_prof[15], 1ull); \
-                if (ix < 8192) { g_trace[ix][0] = r_K; g_trace[ix][1] = clock64() - r_t0; g_trace[ix][2] = r_small; } } } while (0)
-#else
-#define ELA_ROUND_END() do {} while (0)
-#endif
             if (small) {
                 if (!leader) { K = 0; continue; }  // wait at the end of the epsilon
-                PROF_MARK(q0);
                 if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }  // last round's data read everywhere
                 const int bp = ASYNC ? (int)(sr & 1) : 0;
                 Top2<R>* pb = part + (size_t)bp * CS * ELA_SMALL_ROUND;
@@ -1440,7 +1429,6 @@ auction_cluster_kernel(const Params p) {
                         cluster.map_shared_rank(pb, lane)[rank * ELA_SMALL_ROUND + k] = tt;
                     }
                 }
-                PROF_MARK(q1);
                 if (ASYNC) {
                     if (tid == 0) s_fail = !mbar_wait(&s_mbar[bp], (sr >> 1) & 1u, p.wait_ns);
                     __syncthreads();
@@ -1464,12 +1452,10 @@ auction_cluster_kernel(const Params p) {
                         const int j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
                         lbid[k] = add_rn(P[j1], add_rn(sub_rn(tt.v1, tt.v2), eps));
                         lrow[k] = act[k];
-                        lcol[k] = j1;
+                        lcol[k] = (IX)j1;
                     }
                 }
-                PROF_MARK(q2);
                 __syncthreads();
-                PROF_MARK(q3);
                 if (!ASYNC) { cluster_arrive_release(); cl_pending = true; }  // the partials are consumed
                 rounds++;
                 rowbids += K;
@@ -1483,14 +1469,14 @@ auction_cluster_kernel(const Params p) {
                             if (lcol[f] == j) { const U bf = BT::to(lbid[f]); mb = bf > mb ? bf : mb; }
                         int wrow = -1;
                         for (int f = 0; f < K; ++f)
-                            if (lcol[f] == j && absval(sub_rn(lbid[f], BT::from(mb))) < tol) wrow = max(wrow, lrow[f]);
+                            if (lcol[f] == j && absval(sub_rn(lbid[f], BT::from(mb))) < tol) wrow = max(wrow, (int)lrow[f]);
                         if (valid) {
                             int ev = -2;  // lost: bids again
-                            if (wrow == lrow[lane]) {
+                            if (wrow == (int)lrow[lane]) {
                                 const int prev = owner[j];
-                                if (prev >= 0) rowcol[prev] = -1;
+                                if (prev >= 0) rowcol[prev] = (IX)-1;
                                 owner[j] = lrow[lane];
-                                rowcol[lrow[lane]] = j;
+                                rowcol[lrow[lane]] = (IX)j;
                                 P[j] = BT::from(mb);
                                 ev = prev;  // -1: took a free column
                             }
@@ -1498,12 +1484,12 @@ auction_cluster_kernel(const Params p) {
                         }
                         __syncwarp();
                     }
-                } else {
-                    for (int e = tid; e < K; e += blockDim.x) atomicMax(&maxb[lcol[e]], BT::to(lbid[e]));
+                } else {  // new price = max bid (never below the old price), in place
+                    for (int e = tid; e < K; e += blockDim.x) atomicMax(&Pbits[lcol[e]], BT::to(lbid[e]));
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) {
                         const int j = lcol[e];
-                        if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[e] + 1);
+                        if (absval(sub_rn(lbid[e], P[j])) < tol) atomicMax(&win[j], (int)lrow[e] + 1);
                     }
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) {
@@ -1511,16 +1497,15 @@ auction_cluster_kernel(const Params p) {
                         int ev = -2;
                         if (win[j] == i + 1) {
                             const int prev = owner[j];
-                            if (prev >= 0) rowcol[prev] = -1;
-                            owner[j] = i;
-                            rowcol[i] = j;
-                            P[j] = BT::from(maxb[j]);
+                            if (prev >= 0) rowcol[prev] = (IX)-1;
+                            owner[j] = (IX)i;
+                            rowcol[i] = (IX)j;
                             ev = prev;
                         }
                         evict[e] = ev;
                     }
                     __syncthreads();
-                    for (int e = tid; e < K; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
+                    for (int e = tid; e < K; e += blockDim.x) win[lcol[e]] = 0;
                 }
                 // ---- next round: losers, and rows evicted by winners, in entry order
                 if (warp == 0) {
@@ -1528,40 +1513,27 @@ auction_cluster_kernel(const Params p) {
                     for (int e0 = 0; e0 < K; e0 += 32) {
                         const int e = e0 + lane;
                         int r = -1;
-                        if (e < K) r = (evict[e] == -2) ? lrow[e] : evict[e];
+                        if (e < K) r = (evict[e] == -2) ? (int)lrow[e] : evict[e];
                         const unsigned m = __ballot_sync(0xffffffffu, r >= 0);
-                        if (r >= 0) act[pos + __popc(m & ((1u << lane) - 1))] = r;
+                        if (r >= 0) act[pos + __popc(m & ((1u << lane) - 1))] = (IX)r;
                         pos += __popc(m);
                     }
                     if (lane == 0) s_cnt = pos;
                 }
                 __syncthreads();
-                PROF_MARK(q4);
-#ifdef ELA_PROF
-                if (leader && rank == 0 && tid == 0) {
-                    atomicAdd(&g_prof[0], (unsigned long long)(q1 - q0)); atomicAdd(&g_prof[1], (unsigned long long)(q2 - q1));
-                    atomicAdd(&g_prof[2], (unsigned long long)(q3 - q2)); atomicAdd(&g_prof[3], (unsigned long long)(q4 - q3));
-                    atomicAdd(&g_prof[4], 1ull); atomicAdd(&g_prof[5], (unsigned long long)(q0 - r_t0));
-                }
-#endif
                 K = s_cnt;
                 ++it;
-                ELA_ROUND_END();
                 continue;
             }
-            // ================= large round: rows split over the whole team
-            if (tid == 0) { s_cnt = 0; s_total = 0; s_extra = 0; s_fail = 0; }
-            __syncthreads();
-            for (int q = tid; q < my_rows; q += blockDim.x)
-                if (rowcol[row0 + q] < 0) act[atomicAdd(&s_cnt, 1)] = row0 + q;
-            __syncthreads();
-            const int Kl = s_cnt;
+            // ================= large round: the K active rows (ascending in act[])
+            //                   dealt round-robin over the team's CTAs
+            if (tid == 0) { s_total = 0; s_extra = 0; s_fail = 0; }
+            const int Kl = (K > gi) ? (K - 1 - gi) / ST + 1 : 0;  // rows gi, gi+ST, ... of act[]
             const unsigned int t1 = t + 1;
             unsigned long long* myseg =
                 reinterpret_cast<unsigned long long*>(tb + (size_t)((t & 1) * ST + gi) * p.seg_bytes);
-            // one warp per row (rows are many in large rounds)
-            for (int k = warp; k < Kl; k += nw) {
-                const int i = act[k];
+            for (int k = warp; k < Kl; k += nw) {  // one warp per row
+                const int i = act[gi + k * ST];
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
                 if (s_exact) {  // tie-heavy rows: one exact pass
@@ -1575,7 +1547,7 @@ auction_cluster_kernel(const Params p) {
                 R bid;
                 finish_bid<In, R>(p, row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
                 if (lane == 0) {
-                    if (TC == 1) { const int slot = rank * rpc + k; lbid[slot] = bid; lrow[slot] = i; lcol[slot] = j1; }
+                    if (TC == 1) { const int slot = rank * rpc + k; lbid[slot] = bid; lrow[slot] = (IX)i; lcol[slot] = (IX)j1; }
                     else put_entry<R>(myseg, k, t1, i, j1, bid);
                 }
             }
@@ -1609,7 +1581,6 @@ auction_cluster_kernel(const Params p) {
             } else {
                 // ---- exchange through tagged words in global memory (every
                 //      word carries the tag; readers re-read stale words)
-                __syncthreads();
                 if (tid == 0) st_relaxed_u64(myseg, ((unsigned long long)t1 << 32) | (unsigned int)Kl);
                 if (tid < ST) {
                     const unsigned long long* seg =
@@ -1652,15 +1623,15 @@ auction_cluster_kernel(const Params p) {
                                 int rr, cc;
                                 R bb;
                                 decode_entry<R>(w + 1 + Ex<R>::EW * k, rr, cc, bb);
-                                lbid[off + k] = bb; lrow[off + k] = rr; lcol[off + k] = cc;
+                                lbid[off + k] = bb; lrow[off + k] = (IX)rr; lcol[off + k] = (IX)cc;
                             }
                     }
                 }
                 __syncthreads();
                 if (s_fail) { if (cl_pending) cluster_wait_acquire(); cluster.sync(); return; }
-                if (s_extra && !read_extra_entries<R>(tb + (size_t)((t & 1) * ST) * p.seg_bytes, p.seg_bytes, ST,
-                                                      s_segcnt, s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag,
-                                                      p.status)) {
+                if (s_extra && !read_extra_entries<R, IX>(tb + (size_t)((t & 1) * ST) * p.seg_bytes, p.seg_bytes, ST,
+                                                          s_segcnt, s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag,
+                                                          p.status)) {
                     if (cl_pending) cluster_wait_acquire();
                     cluster.sync();
                     return;
@@ -1678,15 +1649,17 @@ auction_cluster_kernel(const Params p) {
                 while (e >= s_off[r + 1]) ++r;
                 return r * rpc + (e - s_off[r]);
             };
+            // the new price of a column is its max bid (bids never fall below
+            // the old price), written in place
             for (int e = tid; e < nent; e += blockDim.x) {
                 const int sl = slot_of(e);
-                atomicMax(&maxb[lcol[sl]], BT::to(lbid[sl]));
+                atomicMax(&Pbits[lcol[sl]], BT::to(lbid[sl]));
             }
             __syncthreads();
             for (int e = tid; e < nent; e += blockDim.x) {
                 const int sl = slot_of(e);
                 const int j = lcol[sl];
-                if (absval(sub_rn(lbid[sl], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[sl] + 1);
+                if (absval(sub_rn(lbid[sl], P[j])) < tol) atomicMax(&win[j], (int)lrow[sl] + 1);
             }
             __syncthreads();
             for (int e = tid; e < nent; e += blockDim.x) {
@@ -1694,35 +1667,18 @@ auction_cluster_kernel(const Params p) {
                 const int j = lcol[sl], i = lrow[sl];
                 if (win[j] == i + 1) {
                     const int prev = owner[j];
-                    if (prev >= 0) rowcol[prev] = -1;
-                    owner[j] = i;
-                    rowcol[i] = j;
-                    P[j] = BT::from(maxb[j]);
+                    if (prev >= 0) rowcol[prev] = (IX)-1;
+                    owner[j] = (IX)i;
+                    rowcol[i] = (IX)j;
                 }
             }
             __syncthreads();
-            for (int e = tid; e < nent; e += blockDim.x) {
-                const int sl = slot_of(e);
-                maxb[lcol[sl]] = 0;
-                win[lcol[sl]] = 0;
-            }
+            for (int e = tid; e < nent; e += blockDim.x) win[lcol[slot_of(e)]] = 0;
             if (TC == 1) { cluster_arrive_release(); cl_pending = true; }  // the bids are consumed
             ++it;
-            // ---- unassigned rows after the round; few -> small rounds
-            if (tid == 0) s_cnt = 0;
-            __syncthreads();
-            {
-                int mine = 0;
-                for (int i = tid; i < N; i += blockDim.x) mine += (rowcol[i] < 0);
-                if (mine) atomicAdd(&s_cnt, mine);
-            }
-            __syncthreads();
-            K = s_cnt;
-            if (small_ok && K <= ELA_SMALL_ROUND && K > 0) {
-                small = true;
-                K = compact_unassigned(rowcol, N, act, s_scan);
-            }
-            ELA_ROUND_END();
+            // ---- next round's bidders (ascending); few -> small rounds
+            K = compact_unassigned(rowcol, N, act, s_scan);
+            if (small_ok && K <= ELA_SMALL_ROUND) small = true;
         }
         // ---- outputs of problem b (CTA 0 of the leader cluster); every CTA of
         //      the cluster is done with this problem's shared data
@@ -1733,8 +1689,9 @@ auction_cluster_kernel(const Params p) {
         if (leader && rank == 0) {
             int un = 0;
             for (int i = tid; i < N; i += blockDim.x) {
-                p.assign_out[b * p.N + i] = rowcol[i];
-                un += (rowcol[i] < 0);
+                const int a = rowcol[i];
+                p.assign_out[b * p.N + i] = a;
+                un += (a < 0);
             }
             R* pout = reinterpret_cast<R*>(p.prices_out) + b * p.M;
             for (int j = tid; j < M; j += blockDim.x) pout[j] = P[j];
@@ -1766,6 +1723,7 @@ struct Plan {
     int path;          // ELA_PATH_CTA / GRID / CLUSTER
     int cs, nclusters; // cluster path: cluster size, clusters launched
     int team;          // cluster path: clusters per problem
+    int idx16;         // cluster path: 16-bit row/column indices in shared memory
     size_t team_bytes; // cluster path: workspace per team
     int S, ngroups, rpc;
     size_t smem;       // dynamic shared memory per CTA
@@ -1798,29 +1756,22 @@ int ctas_per_problem(int64_t B, int64_t N, int sms, int& ngroups) {
     return S < 2 ? 2 : S;
 }
 
-// Largest cluster size (16, else 8) for which at least one cluster of the
-// auction_cluster_kernel<R,R> fits with `smem` bytes per CTA; 0 if none.
-template <typename R>
-int cluster_fit(size_t smem, int& max_clusters) {
-    auto kern = auction_cluster_kernel<R, R>;
-    max_clusters = 0;
+// Clusters of `cs` CTAs of auction_cluster_kernel<R,R,IX> that fit at once with
+// `smem` bytes per CTA (0 if the size is refused).
+template <typename R, typename IX>
+int cluster_fit(int cs, size_t smem) {
+    auto kern = auction_cluster_kernel<R, R, IX>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess) return 0;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) return 0;
-    for (int cs = 16; cs >= 8; cs /= 2) {
-        cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
-        attr[0].id = cudaLaunchAttributeClusterDimension;
-        attr[0].val.clusterDim.x = cs; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-        cfg.gridDim = dim3(cs); cfg.blockDim = dim3(ELA_THREADS_MULTI); cfg.dynamicSmemBytes = smem;
-        cfg.attrs = attr; cfg.numAttrs = 1;
-        int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) == cudaSuccess && n > 0) {
-            max_clusters = n;
-            return cs;
-        }
-        cudaGetLastError();  // clear a refusal of this cluster size
-    }
-    return 0;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+    cfg.gridDim = dim3(cs); cfg.blockDim = dim3(ELA_THREADS_MULTI); cfg.dynamicSmemBytes = smem;
+    cfg.attrs = attr; cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess) { cudaGetLastError(); return 0; }
+    return n;
 }
 
 template <typename R>
@@ -1833,20 +1784,40 @@ int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_
     const size_t multi_smem = k_layout<R>(N, M, rpc, ELA_THREADS_MULTI / 32).total;
     const bool multi_fits = multi_smem <= smem_max && N < (1 << 24) && M < (1 << 24) && N >= 2;
 
-    // cluster plan (sizes only; the largest cluster size the device accepts)
+    // cluster plan: 16-CTA clusters when every problem gets one at once, else
+    // 8-CTA clusters (more of them fit); 16-bit indices below 32768 rows/columns
     int cs = 0, max_clusters = 0;
     size_t cl_smem = 0;
     bool cl_fits = false;
+    const bool idx16 = N < 32768 && M < 32768;
     const bool no_cluster = (path == -1);
     if (no_cluster) path = ELA_PATH_AUTO;
     if (!no_cluster && M >= ELA_SMALL_M && N >= 2 && N < (1 << 24) &&
         (path == ELA_PATH_AUTO || path == ELA_PATH_CLUSTER)) {
-        cl_smem = c_layout<R>(N, M, 16).total;
-        if (cl_smem <= smem_max) cs = cluster_fit<R>(cl_smem, max_clusters);
-        if (cs == 8) {
-            cl_smem = c_layout<R>(N, M, 8).total;
-            if (cl_smem > smem_max) cs = 0;
+        // the largest cluster size that keeps at least 3/4 of the SMs busy
+        // that the best size would (teams of clusters per problem): large
+        // clusters make small rounds faster, more SMs make large rounds faster
+        int force = 0;
+        if (const char* env = getenv("ELA_CLUSTER_SIZE")) force = atoi(env);  // tuning knob
+        int csz[4], ncl[4];
+        size_t smz[4];
+        long used[4], best_used = 0;
+        int nc = 0;
+        for (int c : {16, 8, 4, 2}) {
+            if (force && c != force) continue;
+            const size_t sm = idx16 ? c_layout<R, short>(N, M, c).total : c_layout<R, int>(N, M, c).total;
+            if (sm > smem_max) continue;
+            const int n = idx16 ? cluster_fit<R, short>(c, sm) : cluster_fit<R, int>(c, sm);
+            if (n <= 0) continue;
+            const long teams = B < n ? B : n;
+            const long team = (B < n) ? n / B : 1;
+            const long waves = (B + teams - 1) / teams;
+            csz[nc] = c; ncl[nc] = n; smz[nc] = sm; used[nc] = B * team * c / waves;  // busy SMs per wave
+            if (used[nc] > best_used) best_used = used[nc];
+            ++nc;
         }
+        for (int k = 0; k < nc; ++k)
+            if (4 * used[k] >= 3 * best_used) { cs = csz[k]; max_clusters = ncl[k]; cl_smem = smz[k]; break; }
         cl_fits = cs > 0;
     }
 
@@ -1862,6 +1833,7 @@ int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_
     if (chosen == ELA_PATH_CLUSTER) {
         if (!cl_fits) return ELA_ERR_UNSUPPORTED;
         pl.cs = cs;
+        pl.idx16 = idx16 ? 1 : 0;
         // few problems: a team of clusters per problem shares its large rounds
         int team = 1, nteams = max_clusters;
         if (B < max_clusters) { nteams = (int)B; team = max_clusters / (int)B; }
@@ -1930,7 +1902,7 @@ template <typename In, typename R>
 int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
     if (pl.path == ELA_PATH_CLUSTER) {
         if (!p.vec_ok) return ELA_ERR_UNSUPPORTED;  // rows must allow 16-byte loads
-        auto kern = auction_cluster_kernel<In, R>;
+        auto kern = pl.idx16 ? auction_cluster_kernel<In, R, short> : auction_cluster_kernel<In, R, int>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
