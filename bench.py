@@ -4,9 +4,13 @@ Workload: B=1, N=M=4096 fp32 uniform[0,1) costs (seed 1),
 epsilon scaling 1.0 -> 1e-2 by 0.25 ([1, .25, .0625, .015625, .01]), max_iter
 1000 per epsilon.  One step = one full solve.  With --gpus N (one process per
 GPU under torchrun) every rank solves its own replica (a single problem does
-not split across GPUs), and the batched config 4 (B=256, N=M=512, low-rank +
-noise) is additionally sharded over the ranks (256/N problems each) and
-reported under "batched".
+not split across GPUs).  Also reported, each on its own line key:
+  "fixed_eps": the same matrix with the reference's constant epsilon 1e-2;
+  "batched":   config 4 (B=256, N=M=512, low-rank + noise) sharded over the
+               ranks (256/N problems each);
+  "cfg5":      config 5 (B=8, N=M=8192 bf16 integer costs, eps 1/8193,
+               1000 rounds; the bandwidth-bound case) sharded 8/N per rank,
+               with its own HBM roofline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -44,6 +48,7 @@ def parse():
     ap.add_argument("--no-batched", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
+    ap.add_argument("--no-cfg5", action="store_true", help="skip the bandwidth-bound config-5 leg")
     ap.add_argument("--fixed-eps", action="store_true",
                     help="reference mode: constant epsilon 1e-2 instead of the cfg2 epsilon schedule")
     return ap.parse_args()
@@ -265,6 +270,64 @@ def main():
                    "ms_per_step": round(bm, 4), "value": round(B4 / (bm * 1e-3), 2), "unit": "solves/sec",
                    "scaling": "strong"}
 
+    # the reference's own mode on the cfg2 matrix: constant epsilon 1e-2
+    fixed = None
+    if not args.fixed_eps:
+        for _ in range(args.warmup):
+            rf = ela.auction_solve_op(cost, [1e-2], 1000, ela.PATH_AUTO)
+        f_ms = []
+        for _ in range(args.steps):
+            flush.zero_()
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            rf = ela.auction_solve_op(cost, [1e-2], 1000, ela.PATH_AUTO)
+            s1.record(stream)
+            torch.cuda.synchronize()
+            f_ms.append(s0.elapsed_time(s1))
+        ela._lib.check(int(rf[3].item()), "constant-epsilon solve")
+        fm = max_over_ranks(statistics.mean(f_ms))
+        fixed = {"workload": "cfg2 matrix, constant eps 1e-2 (the reference's only mode), max_iter 1000",
+                 "ms_per_solve": round(fm, 4), "rounds": int(rf[2][0, 0].item()), "row_bids": int(rf[2][0, 1].item())}
+
+    # config 5 (bandwidth-bound: integer costs, bf16, 1000 rounds of price war),
+    # its 8 problems sharded over the ranks
+    cfg5 = None
+    if not args.no_cfg5:
+        from efficient_linear_assignment_b200.sharding import shard_range
+        B5, N5 = 8, 8192
+        lo, hi = shard_range(B5, world, rank)
+        c5 = ela.workloads.cfg5(B5, N5)[lo:hi].contiguous().to(dev)
+        eps5 = [1.0 / (N5 + 1)]
+        r5 = ela.auction_solve_op(c5, eps5, 1000, ela.PATH_AUTO)
+        torch.cuda.synchronize()
+        m5 = []
+        barrier()
+        for _ in range(max(1, min(args.steps, 5))):
+            s0 = torch.cuda.Event(enable_timing=True)
+            s1 = torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            r5 = ela.auction_solve_op(c5, eps5, 1000, ela.PATH_AUTO)
+            s1.record(stream)
+            torch.cuda.synchronize()
+            m5.append(s0.elapsed_time(s1))
+        barrier()
+        ela._lib.check(int(r5[3].item()), "cfg5 solve")
+        bids5 = torch.tensor([float(r5[2][:, 1].sum().item())], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(bids5)
+        ms5 = max_over_ranks(statistics.mean(m5))
+        alg5 = bids5.item() * N5 * 2  # row-bids x M x 2 B (bf16)
+        ach5 = alg5 / (ms5 * 1e-3) / 1e9
+        cfg5 = {"workload": "cfg5: B=8 N=M=8192 bf16 integer costs {0..15}, 5% zero rows, 5% constant columns, "
+                            "eps 1/8193, max_iter 1000 (matrix 1 GB > L2)",
+                "problems_per_gpu": hi - lo, "ms_per_step": round(ms5, 3),
+                "value": round(B5 / (ms5 * 1e-3), 3), "unit": "solves/sec", "scaling": "strong",
+                "unassigned_rows": int(r5[2][:, 3].sum().item()),
+                "roofline": {"bound": "hbm", "achieved": round(ach5, 1), "peak": peak, "unit": "GB/s",
+                             "frac": round(ach5 / peak / world, 4), "alg_bytes_per_step": int(alg5),
+                             "note": "frac per GPU: achieved / (peak x GPUs)"}}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -277,7 +340,7 @@ def main():
             "metric": METRIC, "value": round(value, 5), "unit": "ms/solve", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
             "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic (seeded uniform[0,1), seed 1; cfg4 seed 3)",
+            "data": "synthetic (seeded uniform[0,1), seed 1; cfg4 seed 3; cfg5 seed 4)",
             "config": {"workload": ("cfg2 (fixed eps 1e-2): B=1 N=M=4096 fp32, max_iter 1000" if args.fixed_eps else
                                     "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps"),
                        "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) between steps",
@@ -290,7 +353,9 @@ def main():
             "e2e": None if e2e_val is None else {"value": round(e2e_val, 4), "unit": "ms/solve",
                     "h2d_bytes_per_step": cost_cpu.numel() * 4, "d2h_bytes_per_step": N_MAIN * 8},
             "gpu_launches": args.steps,
+            "fixed_eps": fixed,
             "batched": batched,
+            "cfg5": cfg5,
             "clocks": clk.summary(),
         }
         print(json.dumps(line), flush=True)
