@@ -81,3 +81,23 @@ def test_unaligned_rows_use_scalar_loads(oracle_mod):
     a, p, _ = ela.solve(cost.cuda(), 1e-3, 1000)
     ao, po, _ = oracle_mod.solve(cost.contiguous(), 1e-3, 1000)
     assert torch.equal(a.cpu(), ao) and torch.equal(p.cpu(), po)
+
+
+@pytest.mark.parametrize("cs", [16, 8, 4, 2])
+@pytest.mark.parametrize("team", ["1", "auto"])
+def test_cluster_shapes_vs_oracle(cs, team, monkeypatch, oracle_mod):
+    """Every cluster size, with one cluster per problem (bids over distributed
+    shared memory) and with teams of clusters (bids over global memory)."""
+    monkeypatch.setenv("ELA_CLUSTER_SIZE", str(cs))
+    if team == "1":
+        monkeypatch.setenv("ELA_CLUSTERS_PER_PROBLEM", "1")
+    cases = [
+        (ela.workloads.uniform(1, 1024, 1024, seed=21), 1e-3),            # large then small rounds
+        (ela.workloads.uniform(3, 256, 264, seed=22, dtype=torch.bfloat16), 1e-2),
+        (ela.workloads.cfg5(2, 512), [16.0, 1.0, 1.0 / 513]),            # tie-heavy, epsilon schedule
+    ]
+    for cost, eps in cases:
+        a, p, st = gpu_solve(cost, eps, 1000, ela.PATH_CLUSTER)
+        ao, po, so = oracle_mod.solve(cost, eps, 1000, nthreads=4)
+        assert torch.equal(a, ao) and torch.equal(p, po)
+        assert torch.equal(st[:, :2], so[:, :2])
