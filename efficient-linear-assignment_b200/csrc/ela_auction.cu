@@ -128,30 +128,12 @@ template <> struct Elem<double> {
     template <typename R> static __device__ __forceinline__ R one(const double* p) { return (R)__ldg(p); }
 };
 
-// 16-byte streaming load through the read-only path; the cost matrix is never
-// written during a solve.
+// 16-byte load through the read-only path (the cost matrix is never written
+// during a solve).  Lines may stay in L1: a CTA re-reads the rows it owns,
+// and in small rounds the same column slices, round after round.
 __device__ __forceinline__ uint4 ld_stream16(const void* ptr) {
     uint4 r;
-#if defined(ELA_LD_CG)
-    asm("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
-#elif defined(ELA_LD_NC_L1)
     asm("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
-#elif defined(ELA_LD_CA)
-    asm("ld.global.ca.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
-#elif defined(ELA_LD_EVL)
-    unsigned long long pol;
-    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    asm("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr), "l"(pol));
-#elif defined(ELA_LD_NC_L1_EVL)
-    unsigned long long pol;
-    asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-    asm("ld.global.nc.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr), "l"(pol));
-#else
-    asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-        : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(ptr));
-#endif
     return r;
 }
 
@@ -893,21 +875,6 @@ auction_kernel(const Params p) {
                     const In* row = base + (int64_t)i * p.stride_n;
                     Top2<R> tt;
                     top2_init(tt);
-#ifdef ELA_PROF_SPLIT
-                    if (has && wpr == 16 && p.vec_ok) {
-                        constexpr int W = Elem<In>::W;
-                        long long d[2];
-                        const long long a00 = clock64();
-                        for (int rep = 0; rep < 2; ++rep) {
-                            const long long a0 = clock64();
-                            Top2<R> t0; top2_init(t0);
-                            scan_chunks_fast<In, R, 2>(reinterpret_cast<const uint4*>(row), P, sub * 32 + lane, 512, M / W, t0);
-                            tt = top2_warp_fast(t0);
-                            d[rep] = clock64() - a0;
-                        }
-                        if (warp == 0 && lane == 0 && t < 8192) { g_trace[t][11] = a00 - pt1; g_trace[t][7] = d[0]; g_trace[t][4] = d[1]; }
-                    } else
-#endif
                     const bool exact_first = (wpr == 1) && s_exact;  // tie-heavy rows: one exact pass
                     if (has) tt = exact_first ? scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1)
                                               : scan_row_fast<In, R, UNROLL>(p, row, P, lane, sub, wpr);
@@ -994,9 +961,6 @@ auction_kernel(const Params p) {
                                 if (k < cn) ok = ok && entry_tags_ok<R>(w + 1 + Ex<R>::EW * k, t1);
                             if (ok) { cntv = cn; break; }
                         }
-#ifdef ELA_POLL_SLEEP
-                        __nanosleep(ELA_POLL_SLEEP);
-#endif
                         if ((++spins & 15u) == 0) {
                             if (*(volatile int*)abort_flag) break;
                             if (globaltimer_ns() - t0 > p.wait_ns) {
@@ -1086,9 +1050,7 @@ auction_kernel(const Params p) {
                 if (blockIdx.x == 0 && threadIdx.x == 0) {
                     g_trace[t - 1][0] = ntot; g_trace[t - 1][1] = pt1 - pt0; g_trace[t - 1][2] = pt2 - pt1;
                     g_trace[t - 1][3] = pt3 - pt2;
-#if !defined(ELA_SCAN_TWICE) && !defined(ELA_PROF_SPLIT)
                     g_trace[t - 1][4] = pt4 - pt3;
-#endif
                 }
             }
 #endif
