@@ -7,6 +7,8 @@ from .api import BACKENDS, AuctionIMLE, linear_assignment
 from .solver import AuctionB200, auction_solve_op, solve
 from ._lib import AuctionError, PATH_AUTO, PATH_CTA, PATH_GRID, PATH_CLUSTER
 from . import workloads
+from .utils import get_pad_size, pad_input, pad_to_shape, unpad_result
 
 __all__ = ["linear_assignment", "AuctionIMLE", "AuctionB200", "BACKENDS", "solve",
-           "auction_solve_op", "AuctionError", "PATH_AUTO", "PATH_CTA", "PATH_GRID", "PATH_CLUSTER", "workloads"]
+           "auction_solve_op", "AuctionError", "PATH_AUTO", "PATH_CTA", "PATH_GRID", "PATH_CLUSTER", "workloads",
+           "get_pad_size", "pad_input", "pad_to_shape", "unpad_result"]

@@ -38,16 +38,28 @@ def _solver(backend_name: str, epsilon, max_iter: int):
     return BACKENDS[backend_name](epsilon=epsilon, max_iter=max_iter)
 
 
+def _scatter_rows(out: torch.Tensor, assignment: torch.Tensor, value: float) -> None:
+    """out[b, i, assignment[b, i]] += value for every assigned row (-1 rows skipped)."""
+    valid = (assignment >= 0).unsqueeze(2).to(out.dtype)
+    out.scatter_add_(2, assignment.clamp(min=0).unsqueeze(2), valid * value)
+
+
 class AuctionIMLE(torch.autograd.Function):
     """Forward: hard assignment as a one-hot.  Backward: IMLE difference
-    ``P(C + lambda*G) - P(C)`` divided by lambda (reference api.py:49-149)."""
+    ``P(C + lambda*G) - P(C)`` divided by lambda (reference api.py:49-149).
+
+    Only the (B,N) assignment is saved, not the dense forward one-hot, and the
+    gradient is built as one zero fill plus two sparse row scatters (+1/lambda
+    at the target column, -1/lambda at the forward column); the values equal
+    the reference's dense ``(P_target - P_forward) / lambda``.
+    """
 
     @staticmethod
     def forward(ctx, cost_matrix, epsilon, max_iter, backend_name):
         solver = _solver(backend_name, epsilon, max_iter)
         assignment, _ = solver.solve(cost_matrix)
         P = _one_hot(assignment, cost_matrix)
-        ctx.save_for_backward(cost_matrix, P)
+        ctx.save_for_backward(cost_matrix, assignment)
         ctx.epsilon = epsilon
         ctx.max_iter = max_iter
         ctx.backend_name = backend_name
@@ -56,29 +68,50 @@ class AuctionIMLE(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, grad_output):
-        cost_matrix, P_forward = ctx.saved_tensors
+        cost_matrix, assignment_f = ctx.saved_tensors
         lam = ctx.imle_lambda
         target_cost = cost_matrix + lam * grad_output
         solver = _solver(ctx.backend_name, ctx.epsilon, ctx.max_iter)
         assignment_t, _ = solver.solve(target_cost)
-        P_target = _one_hot(assignment_t, cost_matrix)
-        return (P_target - P_forward) / lam, None, None, None
+        grad = torch.zeros_like(cost_matrix)
+        _scatter_rows(grad, assignment_t, 1.0 / lam)
+        _scatter_rows(grad, assignment_f, -1.0 / lam)
+        return grad, None, None, None
 
 
 def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[float]] = 1e-2,
-                      max_iter: int = 1000, backend: str = "b200", return_indices: bool = True):
+                      max_iter: int = 1000, backend: str = "b200", return_indices: bool = True,
+                      auto_pad: bool = False):
     """Solve the linear assignment problem (minimise total cost) by auction.
 
     cost_matrix: (B,N,M) or (N,M) CUDA tensor, fp32/fp16/bf16/fp64, N and M
-    multiples of 8.  epsilon: constant epsilon (the reference's only mode) or an
-    epsilon-scaling schedule.  Returns (B,N) int64 indices when return_indices,
-    else the differentiable (B,N,M) one-hot.
+    multiples of 8 (as in the reference) unless auto_pad.  epsilon: constant
+    epsilon (the reference's only mode) or an epsilon-scaling schedule.
+    Returns (B,N) int64 indices when return_indices, else the differentiable
+    (B,N,M) one-hot.
+
+    auto_pad=True accepts any N and M and returns what solving
+    ``pad_input(cost)`` and keeping the real rows (``unpad_result``) returns.
+    When M needs padding and there are no more dummy rows than dummy columns,
+    the problem is solved as given, without the copy: the dummy columns (cost
+    1e9 for real rows) never enter a real row's top-2 bid, and the dummy rows
+    (cost 0 on dummy columns, 1e9 on real ones) settle on dummy columns, so
+    the real rows' rounds are the same.  Otherwise the reference's dummy rows
+    can bid on real columns, and the padded copy is solved.
     """
     is_batched = cost_matrix.ndim == 3
     if not is_batched:
         cost_matrix = cost_matrix.unsqueeze(0)
     _, N, M = cost_matrix.shape
-    if N % 8 != 0 or M % 8 != 0:
+    if auto_pad and (N % 8 != 0 or M % 8 != 0):
+        from .utils import get_pad_size, pad_input, unpad_result
+        pn, pm = get_pad_size(N), get_pad_size(M)
+        if pm == 0 or pn > pm or M < 2:  # dummy rows could reach real columns: solve the copy
+            padded, shape = pad_input(cost_matrix)
+            out = linear_assignment(padded, epsilon, max_iter, backend, return_indices)
+            out = unpad_result(out, shape) if return_indices else out[:, :N, :M]
+            return out if is_batched else out.squeeze(0)
+    elif N % 8 != 0 or M % 8 != 0:
         raise ValueError(f"Input dimensions must be multiples of 8. Got shape {cost_matrix.shape}. "
                          "Please pad your input.")
     if return_indices:

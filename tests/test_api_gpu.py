@@ -133,3 +133,17 @@ def test_multi_device_sharding_matches_single_solve():
     devs = [torch.device("cuda", i) for i in range(torch.cuda.device_count())]
     a, p = solve_multi_device(cost, devs, lambda c: ela.solve(c, 1e-2)[:2])
     assert torch.equal(a, ref_a) and torch.equal(p, ref_p)
+
+
+@pytest.mark.parametrize("shape", [(2, 13, 21), (1, 16, 21), (1, 13, 16), (3, 7, 9)])
+def test_auto_pad_equals_explicit_padding(shape):
+    """auto_pad returns the real rows of the solve of pad_input(cost)."""
+    B, N, M = shape
+    g = torch.Generator().manual_seed(N * 100 + M)
+    cost = torch.rand(B, N, M, generator=g).to(dev)
+    padded, orig = ela.pad_input(cost)
+    expect = ela.unpad_result(ela.linear_assignment(padded, epsilon=1e-3, max_iter=2000), orig)
+    got = ela.linear_assignment(cost, epsilon=1e-3, max_iter=2000, auto_pad=True)
+    assert torch.equal(got, expect)
+    with pytest.raises(ValueError):
+        ela.linear_assignment(cost, epsilon=1e-3)

@@ -49,3 +49,19 @@ def test_oracle_threads_do_not_change_results(oracle_mod):
     a1, p1, _ = oracle_mod.solve(cost, 1e-2, 1000, nthreads=1)
     a8, p8, _ = oracle_mod.solve(cost, 1e-2, 1000, nthreads=8)
     assert torch.equal(a1, a8) and torch.equal(p1, p8)
+
+
+@pytest.mark.parametrize("shape", [(2, 13, 21), (1, 16, 21), (3, 7, 9), (2, 30, 45), (1, 17, 17)])
+def test_direct_solve_equals_padded_solve_when_dummy_rows_fit(shape, oracle_mod):
+    """The equivalence auto_pad relies on: with M padded and no more dummy rows
+    than dummy columns, the real rows of solve(pad_input(C)) equal solve(C)."""
+    import efficient_linear_assignment_b200 as ela
+    B, N, M = shape
+    pn, pm = ela.get_pad_size(N), ela.get_pad_size(M)
+    assert pm > 0 and pn <= pm
+    g = torch.Generator().manual_seed(N + 7 * M)
+    cost = torch.rand(B, N, M, generator=g)
+    padded, _ = ela.pad_input(cost)
+    ap, _, _ = oracle_mod.solve(padded, 1e-3, 2000)
+    ad, _, _ = oracle_mod.solve(cost, 1e-3, 2000)
+    assert torch.equal(ap[:, :N], ad)
