@@ -41,7 +41,7 @@
 __device__ unsigned long long g_prof[16];
 __device__ unsigned long long g_trace[8192][12];
 #define PROF_MARK(var) long long var = clock64()
-#define PROF_ADDALL(slot, v) do { if (threadIdx.x == 0) atomicAdd(&g_prof[slot], (unsigned long long)(v)); } while (0)
+#define PROF_ADDALL(slot, v) do { if (threadIdx.x == 0 && MULTI) atomicAdd(&g_prof[slot], (unsigned long long)(v)); } while (0)
 #define PROF_ADD(slot, a, b) do { if (blockIdx.x == 0 && threadIdx.x == 0) atomicAdd(&g_prof[slot], (unsigned long long)((b) - (a))); } while (0)
 #else
 #define PROF_MARK(var)
@@ -406,11 +406,21 @@ __device__ __forceinline__ void scan_chunks(const uint4* rv, const R* __restrict
         for (int u = 0; u < UNROLL; ++u) {
             const int ch = base + u * stride;
             if (ch < nchunks) {
-                R x[W], pr[W];
+                R x[W], pr[W], v[W];
                 Elem<In>::template unpack<R>(raw[u], x);
                 load_prices<R, W>(Ps, ch * W, pr);
 #pragma unroll
-                for (int e = 0; e < W; ++e) top2_add(t, sub_rn(-x[e], pr[e]), ch * W + e);
+                for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
+                // a chunk whose maximum is not above the running second value
+                // cannot change the top-2 (a tied maximum is already recorded
+                // whenever v2 == v1), so only such chunks pay per element
+                R cm = v[0];
+#pragma unroll
+                for (int e = 1; e < W; ++e) cm = rmax(cm, v[e]);
+                if (t.p1 < 0 || cm > t.v2) {
+#pragma unroll
+                    for (int e = 0; e < W; ++e) top2_add(t, v[e], ch * W + e);
+                }
             }
         }
     }
@@ -469,10 +479,15 @@ __device__ __forceinline__ void scan_chunks_fast(const uint4* rv, const R* __res
                 load_prices<R, W>(Ps, ch * W, pr);
 #pragma unroll
                 for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
-                R mx, sd;
-                int ix;
-                chunk_top2<R, W>(v, mx, sd, ix);
-                lane_merge(t, mx, sd, ch * W + ix);
+                R cm = v[0];
+#pragma unroll
+                for (int e = 1; e < W; ++e) cm = rmax(cm, v[e]);
+                if (t.p1 < 0 || cm > t.v2) {  // otherwise the chunk cannot change (v1, p1, v2)
+                    R mx, sd;
+                    int ix;
+                    chunk_top2<R, W>(v, mx, sd, ix);
+                    lane_merge(t, mx, sd, ch * W + ix);
+                }
             }
         }
     }
