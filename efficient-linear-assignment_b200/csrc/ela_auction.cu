@@ -780,6 +780,9 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 #endif
 #define ELA_THREADS_MULTI 512
 #define ELA_MINB_MULTI 1
+#ifndef ELA_UNROLL_EXACT
+#define ELA_UNROLL_EXACT 4
+#endif
 #ifndef ELA_UNROLL_MULTI
 #define ELA_UNROLL_MULTI 4
 #endif
@@ -1514,10 +1517,10 @@ auction_cluster_kernel(const Params p) {
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
                 if (s_exact) {  // tie-heavy rows: one exact pass
-                    tt = scan_row<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                    tt = scan_row<In, R, ELA_UNROLL_EXACT>(p, row, P, lane, 0, 1);
                 } else {
                     tt = scan_row_fast<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
-                    if (tt.v1 == tt.v2) tt = scan_row<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
+                    if (tt.v1 == tt.v2) tt = scan_row<In, R, ELA_UNROLL_EXACT>(p, row, P, lane, 0, 1);
                 }
                 if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                 int j1;
