@@ -1561,7 +1561,8 @@ auction_cluster_kernel(const Params p) {
             } else {
                 // ---- exchange through tagged words in global memory (every
                 //      word carries the tag; readers re-read stale words)
-                if (tid == 0) st_relaxed_u64(myseg, ((unsigned long long)t1 << 32) | (unsigned int)Kl);
+                if (tid == 0 && !(p.skip_publish && t == 0 && gi == 0))  // (test hook: CTA 0 withholds round 0)
+                    st_relaxed_u64(myseg, ((unsigned long long)t1 << 32) | (unsigned int)Kl);
                 if (tid < ST) {
                     const unsigned long long* seg =
                         reinterpret_cast<const unsigned long long*>(tb + (size_t)((t & 1) * ST + tid) * p.seg_bytes);

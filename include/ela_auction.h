@@ -100,8 +100,9 @@ void ela_auction_set_wait_limit_ns(uint64_t ns);
 
 /*
  * Test hook for the timeout path.  When `on` is nonzero, CTA 0 of every group
- * of the grid path never publishes its first round's bids, so every CTA's
- * bounded wait for them runs out and the solve ends with ELA_ERR_TIMEOUT
+ * of the grid path, and of every team of clusters of the cluster path, never
+ * publishes its first exchanged round's bids, so every CTA's bounded wait for
+ * them runs out and the solve ends with ELA_ERR_TIMEOUT
  * (no fault, no hang; the CUDA context stays usable).  Process-wide setting.
  */
 void ela_auction_debug_skip_arrive(int on);

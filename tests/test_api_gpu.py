@@ -147,3 +147,22 @@ def test_auto_pad_equals_explicit_padding(shape):
     assert torch.equal(got, expect)
     with pytest.raises(ValueError):
         ela.linear_assignment(cost, epsilon=1e-3)
+
+
+def test_cluster_team_wait_timeout_reports_status(monkeypatch):
+    """The global-memory exchange between the clusters of a team is bounded too."""
+    lib = _lib.load()
+    monkeypatch.setenv("ELA_CLUSTER_SIZE", "4")  # a team of several clusters for one problem
+    cost = ela.workloads.uniform(1, 2048, 2048, seed=6).to(dev)
+    lib.ela_auction_set_wait_limit_ns(20_000_000)
+    lib.ela_auction_debug_skip_arrive(1)
+    try:
+        with pytest.raises(ela.AuctionError) as ei:
+            ela.solve(cost, 1e-2, path=ela.PATH_CLUSTER)
+        assert ei.value.status == _lib.ELA_ERR_TIMEOUT
+    finally:
+        lib.ela_auction_debug_skip_arrive(0)
+        lib.ela_auction_set_wait_limit_ns(2_000_000_000)
+    a, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_CLUSTER)
+    b, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_GRID)
+    assert torch.equal(a, b)
