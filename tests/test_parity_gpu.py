@@ -101,3 +101,27 @@ def test_cluster_shapes_vs_oracle(cs, team, monkeypatch, oracle_mod):
         ao, po, so = oracle_mod.solve(cost, eps, 1000, nthreads=4)
         assert torch.equal(a, ao) and torch.equal(p, po)
         assert torch.equal(st[:, :2], so[:, :2])
+
+
+def test_cfg5_full_size_problem_vs_oracle(oracle_mod):
+    """One 8192 x 8192 bf16 problem of config 5 (integer costs, zero rows,
+    constant columns: ties everywhere; 1000 rounds of price war), bit-exact."""
+    import os
+    cost = ela.workloads.cfg5(8, 8192)[3:4].contiguous()
+    a, p, st = gpu_solve(cost, 1.0 / 8193, 1000, ela.PATH_AUTO)
+    ao, po, so = oracle_mod.solve(cost, 1.0 / 8193, 1000, nthreads=os.cpu_count() or 4)
+    assert torch.equal(a, ao) and torch.equal(p, po)
+    assert torch.equal(st[:, :2], so[:, :2])
+    assert int(st[0, 3]) == int((a == -1).sum())
+
+
+def test_custom_op_traces_under_torch_compile():
+    cost = ela.workloads.uniform(2, 128, 128, seed=9).cuda()
+
+    def f(c):
+        a, p, st, status = ela.auction_solve_op(c, [1e-2], 1000, 0)
+        return a, p
+
+    a0, p0 = f(cost)
+    a1, p1 = torch.compile(f, backend="aot_eager", fullgraph=True)(cost)
+    assert torch.equal(a0, a1) and torch.equal(p0, p1)
