@@ -716,26 +716,50 @@ __device__ bool read_extra_entries(const unsigned char* segbase, size_t seg_byte
     __syncthreads();
     const int total = exoff[S];
     bool ok = true;
-    for (int idx = tid; idx < total && ok; idx += blockDim.x) {
-        int lo = 0, hi = S - 1;  // last segment whose extra entries start at or before idx
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (exoff[mid] <= idx) lo = mid; else hi = mid - 1;
-        }
-        const int k = Ex<R>::INL + (idx - exoff[lo]);
-        const unsigned long long* seg = reinterpret_cast<const unsigned long long*>(segbase + (size_t)lo * seg_bytes);
-        int rr = 0, cc = 0;
-        R bb = (R)0;
-        unsigned int tries = 0;
-        while (!get_entry<R>(seg, k, t1, rr, cc, bb)) {
-            if (++tries > (1u << 22)) {
-                atomicCAS(status, ELA_OK, ELA_ERR_TIMEOUT);
-                atomicExch(abort_flag, 1);
-                ok = false;
-                break;
+    constexpr int BATCH = 4;  // entries per thread whose loads are in flight together
+    for (int b0 = tid; b0 < total && ok; b0 += BATCH * blockDim.x) {
+        int seg_of[BATCH], k_of[BATCH];
+        unsigned long long w[BATCH][Ex<R>::EW];
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+            const int idx = b0 + u * blockDim.x;
+            seg_of[u] = -1;
+            if (idx < total) {
+                int lo = 0, hi = S - 1;  // last segment whose extra entries start at or before idx
+                while (lo < hi) {
+                    const int mid = (lo + hi + 1) >> 1;
+                    if (exoff[mid] <= idx) lo = mid; else hi = mid - 1;
+                }
+                seg_of[u] = lo;
+                k_of[u] = Ex<R>::INL + (idx - exoff[lo]);
+                const unsigned long long* e = reinterpret_cast<const unsigned long long*>(segbase + (size_t)lo * seg_bytes) +
+                                              1 + Ex<R>::EW * k_of[u];
+#pragma unroll
+                for (int q = 0; q < Ex<R>::EW; ++q) w[u][q] = ld_relaxed_u64(e + q);
             }
         }
-        lbid[off[lo] + k] = bb; lrow[off[lo] + k] = (IX)rr; lcol[off[lo] + k] = (IX)cc;
+#pragma unroll
+        for (int u = 0; u < BATCH; ++u) {
+            if (seg_of[u] < 0) continue;
+            const unsigned long long* seg = reinterpret_cast<const unsigned long long*>(segbase + (size_t)seg_of[u] * seg_bytes);
+            int rr = 0, cc = 0;
+            R bb = (R)0;
+            if (entry_tags_ok<R>(w[u], t1)) {
+                decode_entry<R>(w[u], rr, cc, bb);
+            } else {  // not visible yet: re-read this entry until its words carry the tag
+                unsigned int tries = 0;
+                while (!get_entry<R>(seg, k_of[u], t1, rr, cc, bb)) {
+                    if (++tries > (1u << 22)) {
+                        atomicCAS(status, ELA_OK, ELA_ERR_TIMEOUT);
+                        atomicExch(abort_flag, 1);
+                        ok = false;
+                        break;
+                    }
+                }
+            }
+            const int o = off[seg_of[u]] + k_of[u];
+            lbid[o] = bb; lrow[o] = (IX)rr; lcol[o] = (IX)cc;
+        }
     }
     return __syncthreads_and(ok) != 0;
 }
@@ -1507,6 +1531,7 @@ auction_cluster_kernel(const Params p) {
             }
             // ================= large round: the K active rows (ascending in act[])
             //                   dealt round-robin over the team's CTAs
+            PROF_MARK(L0);
             if (tid == 0) { s_total = 0; s_extra = 0; s_fail = 0; }
             const int Kl = (K > gi) ? (K - 1 - gi) / ST + 1 : 0;  // rows gi, gi+ST, ... of act[]
             const unsigned int t1 = t + 1;
@@ -1532,6 +1557,7 @@ auction_cluster_kernel(const Params p) {
                 }
             }
             __syncthreads();
+            PROF_MARK(L1);
             if (tid == 0) { s_exact = (Kl > 0) ? (s_ties * 4 > Kl) : s_exact; s_ties = 0; }
             int nent;
             bool compact;  // entries at 0..nent-1 (else slots rank*rpc + k)
@@ -1621,6 +1647,7 @@ auction_cluster_kernel(const Params p) {
                 compact = true;
                 ++t;
             }
+            PROF_MARK(L2);
             rounds++;
             rowbids += nent;
             // ---- election over all bids (identical in every CTA of the team)
@@ -1656,10 +1683,19 @@ auction_cluster_kernel(const Params p) {
             __syncthreads();
             for (int e = tid; e < nent; e += blockDim.x) win[lcol[slot_of(e)]] = 0;
             if (TC == 1) { cluster_arrive_release(); cl_pending = true; }  // the bids are consumed
+            PROF_MARK(L3);
             ++it;
             // ---- next round's bidders (ascending); few -> small rounds
             K = compact_unassigned(rowcol, N, act, s_scan);
             if (small_ok && K <= ELA_SMALL_ROUND) small = true;
+            PROF_MARK(L4);
+#ifdef ELA_PROF
+            if (leader && rank == 0 && tid == 0 && nent >= 513) {
+                atomicAdd(&g_prof[6], (unsigned long long)(L1 - L0)); atomicAdd(&g_prof[7], (unsigned long long)(L2 - L1));
+                atomicAdd(&g_prof[8], (unsigned long long)(L3 - L2)); atomicAdd(&g_prof[9], (unsigned long long)(L4 - L3));
+                atomicAdd(&g_prof[10], 1ull); atomicAdd(&g_prof[11], (unsigned long long)Kl);
+            }
+#endif
         }
         // ---- outputs of problem b (CTA 0 of the leader cluster); every CTA of
         //      the cluster is done with this problem's shared data
