@@ -459,37 +459,47 @@ __device__ __forceinline__ void lane_merge(Top2<R>& t, R mx, R sd, int col) {
     t.v1 = gt ? mx : t.v1;
 }
 
+#ifndef ELA_UNROLL_FAST
+#define ELA_UNROLL_FAST 4  // loads in flight per lane in the fast scan (8 spills in the cluster kernel)
+#endif
+
+// One 16-byte chunk folded into the lane state, branch-free: with 32 lanes
+// some lane almost always holds a chunk that beats its running second value,
+// so a per-chunk filter branch costs the warp more than it saves.
+template <typename In, typename R>
+__device__ __forceinline__ void fast_chunk(const uint4& raw, const R* __restrict__ Ps, int ch, Top2<R>& t) {
+    constexpr int W = Elem<In>::W;
+    R x[W], pr[W], v[W];
+    Elem<In>::template unpack<R>(raw, x);
+    load_prices<R, W>(Ps, ch * W, pr);
+#pragma unroll
+    for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
+    R mx, sd;
+    int ix;
+    chunk_top2<R, W>(v, mx, sd, ix);
+    lane_merge(t, mx, sd, ch * W + ix);
+}
+
+// Chunks base, base+stride, ... below nchunks.  Whole batches of UNROLL loads
+// run without bounds predicates; the last, partial batch is predicated.
 template <typename In, typename R, int UNROLL>
 __device__ __forceinline__ void scan_chunks_fast(const uint4* rv, const R* __restrict__ Ps, int base, int stride,
                                                  int nchunks, Top2<R>& t) {
-    constexpr int W = Elem<In>::W;
-    for (; base < nchunks; base += stride * UNROLL) {
+    for (; base + (UNROLL - 1) * stride < nchunks; base += stride * UNROLL) {
         uint4 raw[UNROLL];
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int ch = base + u * stride;
-            if (ch < nchunks) raw[u] = ld_stream16(rv + ch);
-        }
+        for (int u = 0; u < UNROLL; ++u) raw[u] = ld_stream16(rv + base + u * stride);
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int ch = base + u * stride;
-            if (ch < nchunks) {
-                R x[W], pr[W], v[W];
-                Elem<In>::template unpack<R>(raw[u], x);
-                load_prices<R, W>(Ps, ch * W, pr);
+        for (int u = 0; u < UNROLL; ++u) fast_chunk<In, R>(raw[u], Ps, base + u * stride, t);
+    }
+    if (UNROLL > 1 && base < nchunks) {
+        uint4 raw[UNROLL > 1 ? UNROLL - 1 : 1];
 #pragma unroll
-                for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
-                R cm = v[0];
+        for (int u = 0; u < UNROLL - 1; ++u)
+            if (base + u * stride < nchunks) raw[u] = ld_stream16(rv + base + u * stride);
 #pragma unroll
-                for (int e = 1; e < W; ++e) cm = rmax(cm, v[e]);
-                if (t.p1 < 0 || cm > t.v2) {  // otherwise the chunk cannot change (v1, p1, v2)
-                    R mx, sd;
-                    int ix;
-                    chunk_top2<R, W>(v, mx, sd, ix);
-                    lane_merge(t, mx, sd, ch * W + ix);
-                }
-            }
-        }
+        for (int u = 0; u < UNROLL - 1; ++u)
+            if (base + u * stride < nchunks) fast_chunk<In, R>(raw[u], Ps, base + u * stride, t);
     }
 }
 
@@ -548,8 +558,8 @@ __device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row,
         const int base = sub * 32 + lane;
         if (per_lane <= 1) scan_chunks_fast<In, R, 1>(rv, Ps, base, stride, nchunks, t);
         else if (per_lane <= 2) scan_chunks_fast<In, R, 2>(rv, Ps, base, stride, nchunks, t);
-        else if (per_lane <= 4 || UNROLL <= 4) scan_chunks_fast<In, R, 4>(rv, Ps, base, stride, nchunks, t);
-        else scan_chunks_fast<In, R, UNROLL>(rv, Ps, base, stride, nchunks, t);
+        else if (per_lane <= 4) scan_chunks_fast<In, R, 4>(rv, Ps, base, stride, nchunks, t);
+        else scan_chunks_fast<In, R, ELA_UNROLL_FAST>(rv, Ps, base, stride, nchunks, t);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
             lane_merge(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), (R)-INFINITY, col);
