@@ -389,40 +389,67 @@ template <typename R, int W> __device__ __forceinline__ void load_prices(const R
     }
 }
 
-// Lane-local top-2 over chunks base, base+stride, ... (UNROLL chunks per
-// batch).  Chunks are 16-byte vectors of W elements.
-template <typename In, typename R, int UNROLL>
+#ifndef ELA_PF_BATCHES
+#define ELA_PF_BATCHES 1  // L2 prefetch distance of the row scans, in batches
+#endif
+
+// L2 prefetch of this warp's chunks PF batches after the batch at `base`
+// (lane's chunk; the warp's chunks of slot u are the 32 consecutive chunks
+// from base - lane + u*stride, i.e. four 128-byte lines).  Lane l < 4*UNROLL
+// takes line l % 4 of slot l / 4.  Costs no registers beyond the address.
+template <int UNROLL, bool PF>
+__device__ __forceinline__ void prefetch_batch(const uint4* rv, int base, int stride, int nchunks) {
+    if (ELA_PF_BATCHES > 0 && PF) {
+        const int lane = threadIdx.x & 31;
+        if (lane < 4 * UNROLL) {
+            const int ch = base - lane + ELA_PF_BATCHES * UNROLL * stride + (lane >> 2) * stride + (lane & 3) * 8;
+            if (ch < nchunks) asm volatile("prefetch.global.L2 [%0];" ::"l"(rv + ch));
+        }
+    }
+}
+
+// One 16-byte chunk added to the lane's exact top-2.  A chunk whose maximum is
+// not above the running second value cannot change it (a tied maximum is
+// already recorded whenever v2 == v1), so only other chunks pay per element.
+template <typename In, typename R>
+__device__ __forceinline__ void exact_chunk(const uint4& raw, const R* __restrict__ Ps, int ch, Top2<R>& t) {
+    constexpr int W = Elem<In>::W;
+    R x[W], pr[W], v[W];
+    Elem<In>::template unpack<R>(raw, x);
+    load_prices<R, W>(Ps, ch * W, pr);
+#pragma unroll
+    for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
+    R cm = v[0];
+#pragma unroll
+    for (int e = 1; e < W; ++e) cm = rmax(cm, v[e]);
+    if (t.p1 < 0 || cm > t.v2) {
+#pragma unroll
+        for (int e = 0; e < W; ++e) top2_add(t, v[e], ch * W + e);
+    }
+}
+
+// Lane-local exact top-2 over chunks base, base+stride, ... below nchunks
+// (16-byte vectors of W elements).  Whole batches of UNROLL loads run without
+// bounds predicates; the last, partial batch is predicated.
+template <typename In, typename R, int UNROLL, bool PF>
 __device__ __forceinline__ void scan_chunks(const uint4* rv, const R* __restrict__ Ps, int base, int stride,
                                             int nchunks, Top2<R>& t) {
-    constexpr int W = Elem<In>::W;
-    for (; base < nchunks; base += stride * UNROLL) {
+    for (; base + (UNROLL - 1) * stride < nchunks; base += stride * UNROLL) {
         uint4 raw[UNROLL];
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int ch = base + u * stride;
-            if (ch < nchunks) raw[u] = ld_stream16(rv + ch);
-        }
+        for (int u = 0; u < UNROLL; ++u) raw[u] = ld_stream16(rv + base + u * stride);
+        prefetch_batch<UNROLL, PF>(rv, base, stride, nchunks);
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) {
-            const int ch = base + u * stride;
-            if (ch < nchunks) {
-                R x[W], pr[W], v[W];
-                Elem<In>::template unpack<R>(raw[u], x);
-                load_prices<R, W>(Ps, ch * W, pr);
+        for (int u = 0; u < UNROLL; ++u) exact_chunk<In, R>(raw[u], Ps, base + u * stride, t);
+    }
+    if (UNROLL > 1 && base < nchunks) {
+        uint4 raw[UNROLL > 1 ? UNROLL - 1 : 1];
 #pragma unroll
-                for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
-                // a chunk whose maximum is not above the running second value
-                // cannot change the top-2 (a tied maximum is already recorded
-                // whenever v2 == v1), so only such chunks pay per element
-                R cm = v[0];
+        for (int u = 0; u < UNROLL - 1; ++u)
+            if (base + u * stride < nchunks) raw[u] = ld_stream16(rv + base + u * stride);
 #pragma unroll
-                for (int e = 1; e < W; ++e) cm = rmax(cm, v[e]);
-                if (t.p1 < 0 || cm > t.v2) {
-#pragma unroll
-                    for (int e = 0; e < W; ++e) top2_add(t, v[e], ch * W + e);
-                }
-            }
-        }
+        for (int u = 0; u < UNROLL - 1; ++u)
+            if (base + u * stride < nchunks) exact_chunk<In, R>(raw[u], Ps, base + u * stride, t);
     }
 }
 
@@ -585,10 +612,9 @@ __device__ __noinline__ Top2<R> scan_row(const Params& p, const In* row, const R
         const int per_lane = (nchunks + stride - 1) / stride;
         const uint4* rv = reinterpret_cast<const uint4*>(row);
         const int base = sub * 32 + lane;
-        if (per_lane <= 1) scan_chunks<In, R, 1>(rv, Ps, base, stride, nchunks, t);
-        else if (per_lane <= 2) scan_chunks<In, R, 2>(rv, Ps, base, stride, nchunks, t);
-        else if (per_lane <= 4 || UNROLL <= 4) scan_chunks<In, R, 4>(rv, Ps, base, stride, nchunks, t);
-        else scan_chunks<In, R, UNROLL>(rv, Ps, base, stride, nchunks, t);
+        if (per_lane <= 1) scan_chunks<In, R, 1, false>(rv, Ps, base, stride, nchunks, t);
+        else if (per_lane <= 2) scan_chunks<In, R, 2, false>(rv, Ps, base, stride, nchunks, t);
+        else scan_chunks<In, R, 4, true>(rv, Ps, base, stride, nchunks, t);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
             top2_add(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), col);
