@@ -1254,34 +1254,30 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int p
 // returns the count (all threads).  Deterministic: ascending row order.
 template <typename IX>
 __device__ int compact_unassigned(const IX* rowcol, int N, IX* act, int* s_scan) {
-    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
-    const int chunk = (N + nt - 1) / nt;
-    const int r0 = tid * chunk, r1 = min(N, r0 + chunk);
-    int mine = 0;
-    for (int i = r0; i < r1; ++i) mine += (rowcol[i] < 0);
-    // exclusive scan of `mine` over the block
-    int x = mine;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, x, off);
-        if (lane >= off) x += y;
+    // Each warp owns a contiguous block of rows (a multiple of 32) and walks it
+    // 32 rows at a time: consecutive lanes read consecutive entries (no bank
+    // conflicts) and a ballot gives the count and each row's slot.
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int per = (((N + nw - 1) / nw) + 31) & ~31;
+    const int r0 = warp * per, r1 = min(N, r0 + per);
+    int cnt = 0;
+    for (int b = r0; b < r1; b += 32) {
+        const int i = b + lane;
+        cnt += __popc(__ballot_sync(0xffffffffu, i < r1 && rowcol[i] < 0));
     }
-    if (lane == 31) s_scan[warp] = x;
+    if (lane == 0) s_scan[warp] = cnt;
     __syncthreads();
-    if (warp == 0) {
-        int w = (lane < nw) ? s_scan[lane] : 0;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, w, off);
-            if (lane >= off) w += y;
-        }
-        if (lane < nw) s_scan[lane] = w;  // inclusive warp totals
+    const unsigned int w = (lane < nw) ? (unsigned int)s_scan[lane] : 0u;
+    int pos = (int)__reduce_add_sync(0xffffffffu, lane < warp ? w : 0u);  // rows of the warps before
+    const int total = (int)__reduce_add_sync(0xffffffffu, w);
+    const unsigned int below = (1u << lane) - 1u;
+    for (int b = r0; b < r1; b += 32) {
+        const int i = b + lane;
+        const bool u = i < r1 && rowcol[i] < 0;
+        const unsigned int m = __ballot_sync(0xffffffffu, u);
+        if (u) act[pos + __popc(m & below)] = (IX)i;
+        pos += __popc(m);
     }
-    __syncthreads();
-    int pos = x - mine + (warp > 0 ? s_scan[warp - 1] : 0);
-    for (int i = r0; i < r1; ++i)
-        if (rowcol[i] < 0) act[pos++] = (IX)i;
-    const int total = s_scan[nw - 1];
     __syncthreads();
     return total;
 }
@@ -1730,6 +1726,11 @@ auction_cluster_kernel(const Params p) {
                 atomicAdd(&g_prof[6], (unsigned long long)(L1 - L0)); atomicAdd(&g_prof[7], (unsigned long long)(L2 - L1));
                 atomicAdd(&g_prof[8], (unsigned long long)(L3 - L2)); atomicAdd(&g_prof[9], (unsigned long long)(L4 - L3));
                 atomicAdd(&g_prof[10], 1ull); atomicAdd(&g_prof[11], (unsigned long long)Kl);
+            }
+            if (b == 0 && leader && rank == 0 && tid == 0 && it - 1 < 8192) {  // per-round trace of problem 0
+                g_trace[it - 1][0] = nent; g_trace[it - 1][1] = L1 - L0; g_trace[it - 1][2] = L2 - L1;
+                g_trace[it - 1][3] = L3 - L2; g_trace[it - 1][4] = L4 - L3; g_trace[it - 1][5] = Kl;
+                g_trace[it - 1][6] = 1;
             }
 #endif
         }
