@@ -1418,6 +1418,7 @@ auction_cluster_kernel(const Params p) {
             const R eps = (R)p.eps[ph];
             if (small) {
                 if (!leader) { K = 0; continue; }  // wait at the end of the epsilon
+                PROF_MARK(S0);
                 if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }  // last round's data read everywhere
                 const int bp = ASYNC ? (int)(sr & 1) : 0;
                 Top2<R>* pb = part + (size_t)bp * CS * ELA_SMALL_ROUND;
@@ -1430,29 +1431,12 @@ auction_cluster_kernel(const Params p) {
                     const uint4* rv = reinterpret_cast<const uint4*>(row);
                     Top2<R> tt;
                     top2_init(tt);
-                    for (int ch = ch0 + lane; ch < ch1; ch += 32) {
-                        const uint4 raw = ld_stream16(rv + ch);
-                        R x[W], pr[W], v[W];
-                        Elem<In>::template unpack<R>(raw, x);
-                        load_prices<R, W>(P, ch * W, pr);
-#pragma unroll
-                        for (int e = 0; e < W; ++e) v[e] = sub_rn(-x[e], pr[e]);
-                        R mx, sd;
-                        int ix;
-                        chunk_top2<R, W>(v, mx, sd, ix);
-                        lane_merge(tt, mx, sd, ch * W + ix);
-                    }
+                    // the lane's chunks of the slice, loaded two at a time
+                    scan_chunks_fast<In, R, 2>(rv, P, ch0 + lane, 32, ch1, tt);
                     tt = top2_warp_fast(tt);
                     if (tt.p1 >= 0 && tt.v1 == tt.v2) {  // tied maximum in the slice: exact columns
                         top2_init(tt);
-                        for (int ch = ch0 + lane; ch < ch1; ch += 32) {
-                            const uint4 raw = ld_stream16(rv + ch);
-                            R x[W], pr[W];
-                            Elem<In>::template unpack<R>(raw, x);
-                            load_prices<R, W>(P, ch * W, pr);
-#pragma unroll
-                            for (int e = 0; e < W; ++e) top2_add(tt, sub_rn(-x[e], pr[e]), ch * W + e);
-                        }
+                        scan_chunks<In, R, 2, false>(rv, P, ch0 + lane, 32, ch1, tt);
                         tt = top2_warp(tt);
                     }
                     if (ASYNC) {
@@ -1465,6 +1449,7 @@ auction_cluster_kernel(const Params p) {
                         cluster.map_shared_rank(pb, lane)[rank * ELA_SMALL_ROUND + k] = tt;
                     }
                 }
+                PROF_MARK(S1);
                 if (ASYNC) {
                     if (tid == 0) s_fail = !mbar_wait(&s_mbar[bp], (sr >> 1) & 1u, p.wait_ns);
                     __syncthreads();
@@ -1478,6 +1463,7 @@ auction_cluster_kernel(const Params p) {
                     cluster_arrive_release();
                     cluster_wait_acquire();
                 }
+                PROF_MARK(S2);
                 // ---- each row's CS partials merged by one warp: column and bid
                 for (int k = warp; k < K; k += nw) {
                     Top2<R> tt;
@@ -1493,34 +1479,12 @@ auction_cluster_kernel(const Params p) {
                 }
                 __syncthreads();
                 if (!ASYNC) { cluster_arrive_release(); cl_pending = true; }  // the partials are consumed
+                PROF_MARK(S3);
                 rounds++;
                 rowbids += K;
-                // ---- election (identical in every CTA of the cluster)
-                if (K <= 16) {  // one warp, no CTA barrier
-                    if (warp == 0) {
-                        const bool valid = lane < K;
-                        const int j = valid ? lcol[lane] : -1;
-                        U mb = 0;
-                        for (int f = 0; f < K; ++f)
-                            if (lcol[f] == j) { const U bf = BT::to(lbid[f]); mb = bf > mb ? bf : mb; }
-                        int wrow = -1;
-                        for (int f = 0; f < K; ++f)
-                            if (lcol[f] == j && absval(sub_rn(lbid[f], BT::from(mb))) < tol) wrow = max(wrow, (int)lrow[f]);
-                        if (valid) {
-                            int ev = -2;  // lost: bids again
-                            if (wrow == (int)lrow[lane]) {
-                                const int prev = owner[j];
-                                if (prev >= 0) rowcol[prev] = (IX)-1;
-                                owner[j] = lrow[lane];
-                                rowcol[lrow[lane]] = (IX)j;
-                                P[j] = BT::from(mb);
-                                ev = prev;  // -1: took a free column
-                            }
-                            evict[lane] = ev;
-                        }
-                        __syncwarp();
-                    }
-                } else {  // new price = max bid (never below the old price), in place
+                // ---- election (identical in every CTA of the cluster):
+                //      new price = max bid (never below the old price), in place
+                {
                     for (int e = tid; e < K; e += blockDim.x) atomicMax(&Pbits[lcol[e]], BT::to(lbid[e]));
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) {
@@ -1543,6 +1507,7 @@ auction_cluster_kernel(const Params p) {
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) win[lcol[e]] = 0;
                 }
+                PROF_MARK(S4);
                 // ---- next round: losers, and rows evicted by winners, in entry order
                 if (warp == 0) {
                     int pos = 0;
@@ -1557,6 +1522,15 @@ auction_cluster_kernel(const Params p) {
                     if (lane == 0) s_cnt = pos;
                 }
                 __syncthreads();
+                PROF_MARK(S5);
+#ifdef ELA_PROF
+                if (b == 0 && rank == 0 && tid == 0) {
+                    atomicAdd(&g_prof[0], (unsigned long long)(S1 - S0)); atomicAdd(&g_prof[1], (unsigned long long)(S2 - S1));
+                    atomicAdd(&g_prof[2], (unsigned long long)(S3 - S2)); atomicAdd(&g_prof[3], (unsigned long long)(S4 - S3));
+                    atomicAdd(&g_prof[5], (unsigned long long)(S5 - S4)); atomicAdd(&g_prof[4], 1ull);
+                    atomicAdd(&g_prof[12], (unsigned long long)K);
+                }
+#endif
                 K = s_cnt;
                 ++it;
                 continue;
