@@ -169,7 +169,7 @@ def profile_case(args):
     torch.cuda.set_device(0)
     c = ela.workloads.cfg5(8, 8192)[:2].contiguous().cuda()
     for _ in range(2):
-        r = ela.auction_solve_op(c, [1.0 / 8193], 50, ela.PATH_AUTO)
+        r = ela.auction_solve(c, [1.0 / 8193], 50, ela.PATH_AUTO)
     torch.cuda.synchronize()
     ela._lib.check(int(r[3].item()), "profile case")
     print(json.dumps({"profile_case": args.profile_case, "row_bids": int(r[2][:, 1].sum().item()),
@@ -203,6 +203,25 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    def timed(fn, n, flush_between=True):
+        """Device ms of n calls of fn, every call bracketed by events on the
+        stream and all enqueued before one synchronisation: the GPU runs ahead
+        of the host (each L2 flush gives the host time to enqueue the next
+        call), so the events bracket device work only, not host-side launch
+        latency.  Returns (list of ms, last result)."""
+        evs, out = [], None
+        for _ in range(n):
+            if flush_between:
+                flush.zero_()
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            out = fn()
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in evs], out
+
     sched = [1e-2] if args.fixed_eps else ela.workloads.CFG2_SCHEDULE
     cost_cpu = ela.workloads.cfg2()
     cost = cost_cpu.to(dev)
@@ -210,7 +229,7 @@ def main():
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        return ela.auction_solve_op(cost, sched, 1000, ela.PATH_AUTO)
+        return ela.auction_solve(cost, sched, 1000, ela.PATH_AUTO)
 
     for _ in range(args.warmup):
         a, p, st, status = step()
@@ -241,6 +260,20 @@ def main():
     alg_bytes = row_bids * N_MAIN * DTYPE_BYTES
     achieved = alg_bytes / (statistics.mean(per_step) * 1e-3) / 1e9
 
+    # the full-matrix bid pass: a one-round solve (all 4096 rows bid against the
+    # whole 64 MB matrix, then one election), L2 flushed before each, so the matrix
+    # comes from HBM
+    r1_ms, r1 = timed(lambda: ela.auction_solve(cost, [sched[0]], 1, ela.PATH_AUTO), args.warmup + args.steps)
+    r1_ms = r1_ms[args.warmup:]
+    ela._lib.check(int(r1[3].item()), "one-round solve")
+    r1_bytes = int(r1[2][0, 1].item()) * N_MAIN * DTYPE_BYTES
+    r1_t = max_over_ranks(statistics.mean(r1_ms))
+    round1 = {"workload": "cfg2 matrix, max_iter 1: one round, every row bids (L2 flushed)",
+              "ms": round(r1_t, 4), "alg_bytes": r1_bytes,
+              "achieved": round(r1_bytes / (r1_t * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+              "frac": round(r1_bytes / (r1_t * 1e-3) / 1e9 / peak, 4),
+              "note": "whole launch (state init + bid pass + election), device time"}
+
     # e2e through the public API: pinned host cost -> device, solve, indices -> pinned host
     host_cost = cost_cpu.pin_memory()
     host_idx = torch.empty((1, N_MAIN), dtype=torch.int64).pin_memory()
@@ -269,19 +302,10 @@ def main():
         per = hi - lo
         c4 = ela.workloads.cfg4()[lo:hi].contiguous().to(dev)
         for _ in range(args.warmup):
-            r4 = ela.auction_solve_op(c4, [1e-2], 1000, ela.PATH_AUTO)
+            r4 = ela.auction_solve(c4, [1e-2], 1000, ela.PATH_AUTO)
         torch.cuda.synchronize()
-        b_ms = []
         barrier()
-        for _ in range(args.steps):
-            flush.zero_()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            r4 = ela.auction_solve_op(c4, [1e-2], 1000, ela.PATH_AUTO)
-            s1.record(stream)
-            torch.cuda.synchronize()
-            b_ms.append(s0.elapsed_time(s1))
+        b_ms, r4 = timed(lambda: ela.auction_solve(c4, [1e-2], 1000, ela.PATH_AUTO), args.steps)
         barrier()
         ela._lib.check(int(r4[3].item()), "batched solve")
         bm = max_over_ranks(statistics.mean(b_ms))
@@ -293,17 +317,8 @@ def main():
     fixed = None
     if not args.fixed_eps:
         for _ in range(args.warmup):
-            rf = ela.auction_solve_op(cost, [1e-2], 1000, ela.PATH_AUTO)
-        f_ms = []
-        for _ in range(args.steps):
-            flush.zero_()
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            rf = ela.auction_solve_op(cost, [1e-2], 1000, ela.PATH_AUTO)
-            s1.record(stream)
-            torch.cuda.synchronize()
-            f_ms.append(s0.elapsed_time(s1))
+            rf = ela.auction_solve(cost, [1e-2], 1000, ela.PATH_AUTO)
+        f_ms, rf = timed(lambda: ela.auction_solve(cost, [1e-2], 1000, ela.PATH_AUTO), args.steps)
         ela._lib.check(int(rf[3].item()), "constant-epsilon solve")
         fm = max_over_ranks(statistics.mean(f_ms))
         fixed = {"workload": "cfg2 matrix, constant eps 1e-2 (the reference's only mode), max_iter 1000",
@@ -318,18 +333,11 @@ def main():
         lo, hi = shard_range(B5, world, rank)
         c5 = ela.workloads.cfg5(B5, N5)[lo:hi].contiguous().to(dev)
         eps5 = [1.0 / (N5 + 1)]
-        r5 = ela.auction_solve_op(c5, eps5, 1000, ela.PATH_AUTO)
+        r5 = ela.auction_solve(c5, eps5, 1000, ela.PATH_AUTO)
         torch.cuda.synchronize()
-        m5 = []
         barrier()
-        for _ in range(max(1, min(args.steps, 5))):
-            s0 = torch.cuda.Event(enable_timing=True)
-            s1 = torch.cuda.Event(enable_timing=True)
-            s0.record(stream)
-            r5 = ela.auction_solve_op(c5, eps5, 1000, ela.PATH_AUTO)
-            s1.record(stream)
-            torch.cuda.synchronize()
-            m5.append(s0.elapsed_time(s1))
+        m5, r5 = timed(lambda: ela.auction_solve(c5, eps5, 1000, ela.PATH_AUTO), max(1, min(args.steps, 5)),
+                       flush_between=False)  # the 1 GB matrix does not fit in L2
         barrier()
         ela._lib.check(int(r5[3].item()), "cfg5 solve")
         bids5 = torch.tensor([float(r5[2][:, 1].sum().item()), float(r5[2][:, 3].sum().item())],
@@ -364,7 +372,8 @@ def main():
             "config": {"workload": ("cfg2 (fixed eps 1e-2): B=1 N=M=4096 fp32, max_iter 1000" if args.fixed_eps else
                                     "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps"),
                        "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) between steps",
-                       "rounds": rounds, "row_bids": row_bids},
+                       "rounds": rounds, "row_bids": row_bids,
+                       "us_per_round": round(ms_step * 1e3 / max(rounds, 1), 3)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic_per_launch(),
                          "peak_kind": peak_kind,
@@ -374,6 +383,7 @@ def main():
                     "h2d_bytes_per_step": cost_cpu.numel() * 4, "d2h_bytes_per_step": N_MAIN * 8},
             "gpu_launches": args.steps,
             "fixed_eps": fixed,
+            "round1": round1,
             "batched": batched,
             "cfg5": cfg5,
             "clocks": clk.summary(),

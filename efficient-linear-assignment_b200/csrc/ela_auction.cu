@@ -30,6 +30,8 @@
 #include <string.h>
 
 #include <mutex>
+#include <string>
+#include <unordered_map>
 #include <type_traits>
 
 #include "ela_auction.h"
@@ -1911,7 +1913,7 @@ int device_limits(int& sms, size_t& smem_max) {
     return ELA_OK;
 }
 
-int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bool allow_cluster = true) {
+int make_plan_uncached(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bool allow_cluster) {
     if (elem_size(dtype) == 0 || B < 0 || N < 0 || M < 0) return ELA_ERR_ARGUMENT;
     if (path < ELA_PATH_AUTO || path > ELA_PATH_CLUSTER) return ELA_ERR_ARGUMENT;
     if (N > 0 && M < 2) return ELA_ERR_ARGUMENT;
@@ -1924,6 +1926,34 @@ int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bo
     const int ask = (!allow_cluster && path == ELA_PATH_AUTO) ? -1 : path;
     return dtype == ELA_DTYPE_F64 ? make_plan_t<double>(B, N, M, ask, sms, smem_max, pl)
                                   : make_plan_t<float>(B, N, M, ask, sms, smem_max, pl);
+}
+
+// Plans are cached per device, sizes, path and tuning-knob settings: planning
+// runs occupancy queries (several CUDA calls), which would otherwise cost more
+// host time per solve than a small problem's whole solve on the GPU.
+std::mutex g_plan_mu;
+std::unordered_map<std::string, Plan> g_plans;
+
+int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bool allow_cluster = true) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ELA_ERR_CUDA;
+    char key[256];
+    auto knob = [](const char* name) { const char* v = getenv(name); return v ? v : "-"; };
+    snprintf(key, sizeof key, "%d|%d|%lld|%lld|%lld|%d|%d|%.16s|%.16s|%.16s", dev, dtype, (long long)B, (long long)N,
+             (long long)M, path, allow_cluster ? 1 : 0, knob("ELA_CTAS_PER_PROBLEM"), knob("ELA_CLUSTER_SIZE"),
+             knob("ELA_CLUSTERS_PER_PROBLEM"));
+    {
+        std::lock_guard<std::mutex> lock(g_plan_mu);
+        auto it = g_plans.find(key);
+        if (it != g_plans.end()) { pl = it->second; return ELA_OK; }
+    }
+    const int rc = make_plan_uncached(dtype, B, N, M, path, pl, allow_cluster);
+    if (rc == ELA_OK) {
+        std::lock_guard<std::mutex> lock(g_plan_mu);
+        if (g_plans.size() >= 4096) g_plans.clear();
+        g_plans.emplace(key, pl);
+    }
+    return rc;
 }
 
 template <typename In, typename R>

@@ -31,13 +31,19 @@ def _as_schedule(epsilon: EpsArg) -> list[float]:
     return sched
 
 
-@torch.library.custom_op("ela::auction_solve", mutates_args=())
-def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int) -> Tuple[
+def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int) -> Tuple[
         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,))."""
+    """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,)).
+
+    The eager implementation: outputs allocated on the cost's device, one call
+    of ``ela_auction_solve`` on the current stream (which also zeroes the status
+    word and the stats), no synchronisation.  ``auction_solve_op`` is the same
+    computation registered as a torch custom op (for torch.compile graphs).
+    """
     if cost.device.type != "cuda":
         raise RuntimeError("ela::auction_solve needs a CUDA tensor (there is no CPU path)")
-    if cost.dtype not in DTYPE_CODE:
+    code = DTYPE_CODE.get(cost.dtype)
+    if code is None:
         raise TypeError(f"unsupported cost dtype {cost.dtype}")
     if cost.dim() != 3:
         raise ValueError("cost must be (B, N, M)")
@@ -46,32 +52,39 @@ def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: 
     lib = _lib.load()
     B, N, M = cost.shape
     dev = cost.device
-    pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
-    with torch.cuda.device(dev):
-        assign = torch.empty((B, N), dtype=torch.int64, device=dev)
-        prices = torch.empty((B, M), dtype=pdt, device=dev)
-        stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
-        status = torch.zeros((1,), dtype=torch.int32, device=dev)
-        code = DTYPE_CODE[cost.dtype]
-        if B == 0 or N == 0:
-            prices.zero_()
-            stats.zero_()
-            return assign, prices, stats, status
-        ws_bytes = lib.ela_auction_workspace_bytes(code, B, N, M, int(path))
-        if ws_bytes == 0:
-            _lib.check(_lib.ELA_ERR_UNSUPPORTED if M >= 2 else _lib.ELA_ERR_ARGUMENT,
-                       f"ela_auction_workspace_bytes(B={B}, N={N}, M={M}, path={path})")
-        ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
-        e = (ctypes.c_double * len(eps))(*eps)
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        rc = lib.ela_auction_solve(
-            ctypes.c_void_p(cost.data_ptr()), code, B, N, M, cost.stride(0), cost.stride(1),
-            e, len(eps), int(max_iter), int(path), ctypes.c_void_p(assign.data_ptr()),
-            ctypes.c_void_p(prices.data_ptr()), ctypes.c_void_p(stats.data_ptr()),
-            ctypes.c_void_p(status.data_ptr()), ctypes.c_void_p(ws.data_ptr()), ws_bytes,
-            ctypes.c_void_p(stream))
-        _lib.check(rc, "ela_auction_solve")
+    pdt = torch.float64 if code == 3 else torch.float32
+    if dev.index is not None and dev.index != torch.cuda.current_device():
+        with torch.cuda.device(dev):
+            return auction_solve(cost, eps, max_iter, path)
+    assign = torch.empty((B, N), dtype=torch.int64, device=dev)
+    prices = torch.empty((B, M), dtype=pdt, device=dev)
+    stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
+    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    if B == 0 or N == 0:
+        prices.zero_()
+        stats.zero_()
+        status.zero_()
+        return assign, prices, stats, status
+    ws_bytes = lib.ela_auction_workspace_bytes(code, B, N, M, int(path))
+    if ws_bytes == 0:
+        _lib.check(_lib.ELA_ERR_UNSUPPORTED if M >= 2 else _lib.ELA_ERR_ARGUMENT,
+                   f"ela_auction_workspace_bytes(B={B}, N={N}, M={M}, path={path})")
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    e = (ctypes.c_double * len(eps))(*eps)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.ela_auction_solve(
+        cost.data_ptr(), code, B, N, M, cost.stride(0), cost.stride(1),
+        e, len(eps), int(max_iter), int(path), assign.data_ptr(),
+        prices.data_ptr(), stats.data_ptr(), status.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+    _lib.check(rc, "ela_auction_solve")
     return assign, prices, stats, status
+
+
+@torch.library.custom_op("ela::auction_solve", mutates_args=())
+def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int) -> Tuple[
+        torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,))."""
+    return auction_solve(cost, eps, max_iter, path)
 
 
 @auction_solve_op.register_fake
@@ -99,7 +112,10 @@ def solve(cost: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path
     sched = _as_schedule(epsilon)
     if any(not (e > 0.0) or e == float("inf") for e in sched):
         raise ValueError("every epsilon must be finite and > 0")
-    assign, prices, stats, status = auction_solve_op(cost.detach(), sched, int(max_iter), int(path))
+    # the custom op while torch.compile traces; the plain call (no dispatcher
+    # overhead) in eager mode
+    fn = auction_solve_op if torch.compiler.is_compiling() else auction_solve
+    assign, prices, stats, status = fn(cost.detach(), sched, int(max_iter), int(path))
     if check:
         st = int(status.item())
         _lib.check(st, "auction kernel")
