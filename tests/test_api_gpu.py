@@ -166,3 +166,20 @@ def test_cluster_team_wait_timeout_reports_status(monkeypatch):
     a, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_CLUSTER)
     b, _, _ = ela.solve(cost, 1e-2, path=ela.PATH_GRID)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("shape,path", [((3, 64, 64), ela.PATH_AUTO), ((1, 1024, 1024), ela.PATH_CLUSTER),
+                                        ((4, 256, 264), ela.PATH_GRID)])
+def test_eager_entry_equals_custom_op(shape, path):
+    """auction_solve (the eager call behind linear_assignment) and the registered
+    ela::auction_solve op are one computation: identical outputs, repeated calls
+    (cached launch plan) included."""
+    cost = ela.workloads.uniform(*shape, seed=sum(shape)).to(dev)
+    eps = [0.1, 1e-2]
+    ref = ela.auction_solve_op(cost, eps, 1000, path)
+    for _ in range(2):
+        got = ela.auction_solve(cost, eps, 1000, path)
+        torch.cuda.synchronize()
+        assert int(got[3].item()) == 0
+        for g, r in zip(got, ref):
+            assert torch.equal(g, r)
