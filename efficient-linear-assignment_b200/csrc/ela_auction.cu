@@ -1485,8 +1485,37 @@ auction_cluster_kernel(const Params p) {
                 rounds++;
                 rowbids += K;
                 // ---- election (identical in every CTA of the cluster):
-                //      new price = max bid (never below the old price), in place
-                {
+                //      new price = max bid (never below the old price), in place.
+                //      Up to 32 bids: entry e is thread e of warp 0, so warp
+                //      barriers order the steps and the next bidders are listed
+                //      in the same pass; more bids use the whole CTA.
+                if (K <= 32) {
+                    if (warp == 0) {
+                        const bool valid = lane < K;
+                        const int j = valid ? (int)lcol[lane] : 0;
+                        if (valid) atomicMax(&Pbits[j], BT::to(lbid[lane]));
+                        __syncwarp();
+                        if (valid && absval(sub_rn(lbid[lane], P[j])) < tol) atomicMax(&win[j], (int)lrow[lane] + 1);
+                        __syncwarp();
+                        int nxt = -1;  // this entry's bidder in the next round
+                        if (valid) {
+                            const int i = lrow[lane];
+                            nxt = i;  // lost: bids again
+                            if (win[j] == i + 1) {
+                                const int prev = owner[j];
+                                if (prev >= 0) rowcol[prev] = (IX)-1;
+                                owner[j] = (IX)i;
+                                rowcol[i] = (IX)j;
+                                nxt = prev;  // -1: took a free column
+                            }
+                        }
+                        __syncwarp();  // every win[] read before it is cleared
+                        if (valid) win[j] = 0;
+                        const unsigned m = __ballot_sync(0xffffffffu, nxt >= 0);
+                        if (nxt >= 0) act[__popc(m & ((1u << lane) - 1))] = (IX)nxt;
+                        if (lane == 0) s_cnt = __popc(m);
+                    }
+                } else {
                     for (int e = tid; e < K; e += blockDim.x) atomicMax(&Pbits[lcol[e]], BT::to(lbid[e]));
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) {
@@ -1508,21 +1537,21 @@ auction_cluster_kernel(const Params p) {
                     }
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) win[lcol[e]] = 0;
+                    // ---- next round: losers, and rows evicted by winners, in entry order
+                    if (warp == 0) {
+                        int pos = 0;
+                        for (int e0 = 0; e0 < K; e0 += 32) {
+                            const int e = e0 + lane;
+                            int r = -1;
+                            if (e < K) r = (evict[e] == -2) ? (int)lrow[e] : evict[e];
+                            const unsigned m = __ballot_sync(0xffffffffu, r >= 0);
+                            if (r >= 0) act[pos + __popc(m & ((1u << lane) - 1))] = (IX)r;
+                            pos += __popc(m);
+                        }
+                        if (lane == 0) s_cnt = pos;
+                    }
                 }
                 PROF_MARK(S4);
-                // ---- next round: losers, and rows evicted by winners, in entry order
-                if (warp == 0) {
-                    int pos = 0;
-                    for (int e0 = 0; e0 < K; e0 += 32) {
-                        const int e = e0 + lane;
-                        int r = -1;
-                        if (e < K) r = (evict[e] == -2) ? (int)lrow[e] : evict[e];
-                        const unsigned m = __ballot_sync(0xffffffffu, r >= 0);
-                        if (r >= 0) act[pos + __popc(m & ((1u << lane) - 1))] = (IX)r;
-                        pos += __popc(m);
-                    }
-                    if (lane == 0) s_cnt = pos;
-                }
                 __syncthreads();
                 PROF_MARK(S5);
 #ifdef ELA_PROF
