@@ -805,7 +805,7 @@ __device__ bool read_extra_entries(const unsigned char* segbase, size_t seg_byte
 // ================================================================== kernel
 // Shared-memory layout (byte offsets), identical on host and device.
 struct KLayout {
-    size_t P, maxb, win, lbid, lrow, lcol, rowcol, rowbid, active, wtop, scr_v, scr_i, total;
+    size_t P, maxb, win, owner, lbid, lrow, lcol, rowcol, rowbid, active, wtop, scr_v, scr_i, total;
 };
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
@@ -816,6 +816,7 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
     L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);   // prices
     L.maxb = o;   o = align_up(o + sizeof(R) * (size_t)M, 16);   // round's column max bid (bits)
     L.win = o;    o = align_up(o + 4 * (size_t)M, 16);           // round's elected row + 1
+    L.owner = o;  o = align_up(o + 4 * (size_t)M, 16);           // one-CTA path: row owning each column
     L.lbid = o;   o = align_up(o + sizeof(R) * (size_t)N, 16);   // round's bids: value
     L.lrow = o;   o = align_up(o + 4 * (size_t)N, 16);           //               row
     L.lcol = o;   o = align_up(o + 4 * (size_t)N, 16);           //               column
@@ -879,6 +880,7 @@ auction_kernel(const Params p) {
     R* P = reinterpret_cast<R*>(smem + L.P);
     U* maxb = reinterpret_cast<U*>(smem + L.maxb);
     int* win = reinterpret_cast<int*>(smem + L.win);
+    int* owner = reinterpret_cast<int*>(smem + L.owner);  // maintained on the one-CTA path only
     R* lbid = reinterpret_cast<R*>(smem + L.lbid);
     int* lrow = reinterpret_cast<int*>(smem + L.lrow);
     int* lcol = reinterpret_cast<int*>(smem + L.lcol);
@@ -900,7 +902,7 @@ auction_kernel(const Params p) {
 
     for (int64_t b = MULTI ? g : blockIdx.x; b < p.B; b += nprob_step) {
         const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
-        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; maxb[j] = 0; win[j] = 0; }
+        for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; maxb[j] = 0; win[j] = 0; owner[j] = -1; }
         for (int q = tid; q < my_rows; q += blockDim.x) { rowcol[q] = -1; rowbid[q] = -1; }
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
@@ -908,8 +910,10 @@ auction_kernel(const Params p) {
         __syncthreads();
         while (ph < p.n_eps) {
             if (it == p.max_iter) {  // round budget of this epsilon used up
-                if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
+                if (++ph < p.n_eps) {  // the next epsilon starts from unassigned rows
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
+                    for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
+                }
                 it = 0;
                 rebuild = true;
                 __syncthreads();
@@ -1082,40 +1086,79 @@ auction_kernel(const Params p) {
             PROF_MARK(pt3);
             if (ntot == 0) {  // nobody bid: this epsilon's solve has converged
                 rebuild = true;
-                if (++ph < p.n_eps)  // the next epsilon starts from unassigned rows
+                if (++ph < p.n_eps) {  // the next epsilon starts from unassigned rows
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
+                    for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
+                }
                 it = 0;
                 __syncthreads();
                 continue;
             }
             rounds++;
             rowbids += ntot;
-            // ---- election, identical in every CTA of the group
-            for (int e = tid; e < ntot; e += blockDim.x) atomicMax(&maxb[lcol[e]], BT::to(lbid[e]));
-            if (tid == 0) s_nact = 0;
-            __syncthreads();
-            for (int e = tid; e < ntot; e += blockDim.x) {
-                const int j = lcol[e];
-                if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[e] + 1);
-            }
-            __syncthreads();
-            for (int q = tid; q < my_rows; q += blockDim.x) {
-                const int jb = rowbid[q];
-                int col = rowcol[q];
-                if (jb >= 0) {
-                    col = (win[jb] == row0 + q + 1) ? jb : -1;
-                    rowbid[q] = -1;
-                } else if (col >= 0 && maxb[col] != 0) {
-                    col = -1;  // someone took the column
+            // ---- election, identical in every CTA of the group.  One CTA per
+            //      problem with up to 32 bids: entry e is thread e of warp 0, warp
+            //      barriers order the steps, and the next bidders (losers, and
+            //      owners of the columns won) come from the entries instead of a
+            //      pass over every row.
+            if (!MULTI && ntot <= 32) {
+                if (warp == 0) {
+                    const bool valid = lane < ntot;
+                    const int j = valid ? lcol[lane] : 0;
+                    const int i = valid ? lrow[lane] : 0;  // row0 == 0 on this path
+                    if (valid) atomicMax(&maxb[j], BT::to(lbid[lane]));
+                    __syncwarp();
+                    if (valid && absval(sub_rn(lbid[lane], BT::from(maxb[j]))) < tol) atomicMax(&win[j], i + 1);
+                    __syncwarp();
+                    int nxt = -1;  // this entry's bidder in the next round
+                    if (valid) {
+                        nxt = i;  // lost: bids again
+                        rowbid[i] = -1;
+                        if (win[j] == i + 1) {
+                            const int prev = owner[j];
+                            if (prev >= 0) rowcol[prev] = -1;
+                            owner[j] = i;
+                            rowcol[i] = j;
+                            nxt = prev;  // -1: took a free column
+                        }
+                        P[j] = BT::from(maxb[j]);
+                    }
+                    __syncwarp();  // every maxb[] / win[] read before they are cleared
+                    if (valid) { maxb[j] = 0; win[j] = 0; }
+                    const unsigned int m = __ballot_sync(0xffffffffu, nxt >= 0);
+                    if (nxt >= 0) active[__popc(m & ((1u << lane) - 1))] = nxt;
+                    if (lane == 0) s_nact = __popc(m);
                 }
-                rowcol[q] = col;
-                if (col < 0) active[atomicAdd(&s_nact, 1)] = q;  // bids next round
+                __syncthreads();
+            } else {
+                // ---- election, identical in every CTA of the group
+                for (int e = tid; e < ntot; e += blockDim.x) atomicMax(&maxb[lcol[e]], BT::to(lbid[e]));
+                if (tid == 0) s_nact = 0;
+                __syncthreads();
+                for (int e = tid; e < ntot; e += blockDim.x) {
+                    const int j = lcol[e];
+                    if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[e] + 1);
+                }
+                __syncthreads();
+                for (int q = tid; q < my_rows; q += blockDim.x) {
+                    const int jb = rowbid[q];
+                    int col = rowcol[q];
+                    if (jb >= 0) {
+                        col = (win[jb] == row0 + q + 1) ? jb : -1;
+                        if (!MULTI && col >= 0) owner[col] = q;
+                        rowbid[q] = -1;
+                    } else if (col >= 0 && maxb[col] != 0) {
+                        col = -1;  // someone took the column
+                    }
+                    rowcol[q] = col;
+                    if (col < 0) active[atomicAdd(&s_nact, 1)] = q;  // bids next round
+                }
+                for (int e = tid; e < ntot; e += blockDim.x) P[lcol[e]] = BT::from(maxb[lcol[e]]);
+                __syncthreads();
+                // cleared before the next round's election; the bid phase's
+                // barriers lie in between
+                for (int e = tid; e < ntot; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
             }
-            for (int e = tid; e < ntot; e += blockDim.x) P[lcol[e]] = BT::from(maxb[lcol[e]]);
-            __syncthreads();
-            // cleared before the next round's election; the bid phase's
-            // barriers lie in between
-            for (int e = tid; e < ntot; e += blockDim.x) { maxb[lcol[e]] = 0; win[lcol[e]] = 0; }
             ++it;
             PROF_MARK(pt4);
             PROF_ADD(0, pt0, pt1); PROF_ADD(1, pt1, pt2); PROF_ADD(2, pt2, pt3); PROF_ADD(3, pt3, pt4);
