@@ -596,6 +596,46 @@ __device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row,
     return top2_warp_fast(t);
 }
 
+// Fast scans of two rows by one warp at once (16-byte aligned rows): the
+// loads of both rows are in flight together, so a warp that owns several rows
+// in a round waits one memory latency per pair instead of per row.  Each row's
+// state is the one scan_row_fast computes.  `two` is warp-uniform.
+template <typename In, typename R>
+__device__ __forceinline__ void scan_rows2_fast(const Params& p, const In* ra, const In* rb, bool two,
+                                                const R* __restrict__ Ps, int lane, Top2<R>& ta, Top2<R>& tb) {
+    constexpr int W = Elem<In>::W, U = 4;
+    const int nchunks = (int)p.M / W;
+    const uint4* va = reinterpret_cast<const uint4*>(ra);
+    const uint4* vb = reinterpret_cast<const uint4*>(rb);
+    top2_init(ta);
+    top2_init(tb);
+    int base = lane;
+    for (; base + (U - 1) * 32 < nchunks; base += 32 * U) {
+        uint4 a[U], b[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) a[u] = ld_stream16(va + base + u * 32);
+        if (two) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) b[u] = ld_stream16(vb + base + u * 32);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) fast_chunk<In, R>(a[u], Ps, base + u * 32, ta);
+        if (two) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) fast_chunk<In, R>(b[u], Ps, base + u * 32, tb);
+        }
+    }
+    for (; base < nchunks; base += 32) {
+        const uint4 a = ld_stream16(va + base);
+        uint4 b = a;
+        if (two) b = ld_stream16(vb + base);
+        fast_chunk<In, R>(a, Ps, base, ta);
+        if (two) fast_chunk<In, R>(b, Ps, base, tb);
+    }
+    ta = top2_warp_fast(ta);
+    if (two) tb = top2_warp_fast(tb);
+}
+
 // Top-2 over the columns of one row that this warp covers: the row's 16-byte
 // chunks are dealt to `wpr` warps in turn (warp `sub` takes chunks
 // sub*32+lane, sub*32+lane+32*wpr, ...).  The batch size follows the number
@@ -951,6 +991,37 @@ auction_kernel(const Params p) {
                 }
                 const int wpr = 1 << lw;
                 const int groups = nw >> lw;
+                // exact tie tracking is needed only when the maximum is tied
+                // and M >= 128 (below that the tie is settled by introselect)
+                const bool exact_ok = M >= ELA_SMALL_M;
+                // a row's bid from its complete top-2: tie re-scan, column, entry
+                auto emit = [&](int k, int q, const In* row, Top2<R> tt) {
+                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1);
+                    if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
+                    int j1;
+                    R bid;
+                    finish_bid<In, R>(p, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
+                    if (lane == 0) {
+                        rowbid[q] = j1;
+                        if (!MULTI) { lbid[k] = bid; lrow[k] = row0 + q; lcol[k] = j1; }
+                        else put_entry<R>(myseg, k, t1, row0 + q, j1, bid);
+                    }
+                };
+                if (lw == 0 && K > nw && !s_exact && p.vec_ok) {
+                    // several rows per warp: two at a time (no CTA barrier in here)
+                    for (int kb = 0; kb < K; kb += 2 * nw) {
+                        const int ka = kb + warp, kb2 = ka + nw;
+                        if (ka >= K) continue;
+                        const bool two = kb2 < K;
+                        const int qa = active[ka], qb = two ? active[kb2] : qa;
+                        const In* ra = base + (int64_t)(row0 + qa) * p.stride_n;
+                        const In* rb = base + (int64_t)(row0 + qb) * p.stride_n;
+                        Top2<R> ta, tb;
+                        scan_rows2_fast<In, R>(p, ra, rb, two, P, lane, ta, tb);
+                        emit(ka, qa, ra, ta);
+                        if (two) emit(kb2, qb, rb, tb);
+                    }
+                } else
                 for (int kb = 0; kb < K; kb += groups) {
                     const int k = kb + (warp >> lw), sub = warp & (wpr - 1);
                     const bool has = k < K;
@@ -965,9 +1036,6 @@ auction_kernel(const Params p) {
 #ifdef ELA_PROF
                     if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][8], (unsigned long long)(clock64() - pt1));
 #endif
-                    // exact tie tracking is needed only when the maximum is tied
-                    // and M >= 128 (below that the tie is settled by introselect)
-                    const bool exact_ok = M >= ELA_SMALL_M;
                     if (wpr > 1) {
                         if (has && lane == 0) wtop[warp] = tt;
                         __syncthreads();
