@@ -169,24 +169,27 @@ template <typename R> __device__ __forceinline__ void top2_add(Top2<R>& t, R v, 
 }
 
 // Merge two disjoint column sets; commutative, so a butterfly leaves every
-// lane with the same result.
+// lane with the same result.  Selects only (no branches), so the lanes of a
+// warp never diverge in the butterflies: the larger maximum keeps its state
+// (its second value raised to the other maximum); equal maxima make a tie whose
+// two columns are the two smallest of the candidates; an empty side (p1 < 0)
+// yields the other side.
 template <typename R> __device__ __forceinline__ Top2<R> top2_merge(Top2<R> a, Top2<R> b) {
-    if (a.p1 < 0) return b;
-    if (b.p1 < 0) return a;
-    if (a.v1 > b.v1) { a.v2 = (a.v2 > b.v1) ? a.v2 : b.v1; return a; }
-    if (b.v1 > a.v1) { b.v2 = (b.v2 > a.v1) ? b.v2 : a.v1; return b; }
-    Top2<R> r;
-    r.v1 = a.v1; r.v2 = a.v1;
+    const bool gt = a.v1 > b.v1, lt = b.v1 > a.v1;
     const int big = 0x7fffffff;
-    if (a.p1 < b.p1) {
-        r.p1 = a.p1;
-        const int ap2 = a.p2 >= 0 ? a.p2 : big;
-        r.p2 = ap2 < b.p1 ? ap2 : b.p1;
-    } else {
-        r.p1 = b.p1;
-        const int bp2 = b.p2 >= 0 ? b.p2 : big;
-        r.p2 = bp2 < a.p1 ? bp2 : a.p1;
-    }
+    const int ap2 = a.p2 >= 0 ? a.p2 : big, bp2 = b.p2 >= 0 ? b.p2 : big;
+    const bool af = a.p1 < b.p1;
+    const int p1e = af ? a.p1 : b.p1;
+    const int q1 = af ? ap2 : bp2, q2 = af ? b.p1 : a.p1;
+    const int p2e = q1 < q2 ? q1 : q2;
+    const R av2 = (a.v2 > b.v1) ? a.v2 : b.v1, bv2 = (b.v2 > a.v1) ? b.v2 : a.v1;
+    Top2<R> r;
+    r.v1 = lt ? b.v1 : a.v1;
+    r.v2 = gt ? av2 : (lt ? bv2 : a.v1);
+    r.p1 = gt ? a.p1 : (lt ? b.p1 : p1e);
+    r.p2 = gt ? a.p2 : (lt ? b.p2 : p2e);
+    r = (b.p1 < 0) ? a : r;
+    r = (a.p1 < 0) ? b : r;
     return r;
 }
 
