@@ -575,7 +575,7 @@ template <> __device__ __forceinline__ Top2<float> top2_warp_fast<float>(Top2<fl
     return r;
 }
 
-template <typename In, typename R, int UNROLL>
+template <typename In, typename R>
 __device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row, const R* __restrict__ Ps,
                                                  int lane, int sub, int wpr) {
     const int M = (int)p.M;
@@ -644,7 +644,7 @@ __device__ __forceinline__ void scan_rows2_fast(const Params& p, const In* ra, c
 // sub*32+lane, sub*32+lane+32*wpr, ...).  The batch size follows the number
 // of chunks per lane, so no predicated-off batch slots are issued.  The
 // result is reduced over the warp.
-template <typename In, typename R, int UNROLL>
+template <typename In, typename R>
 __device__ __noinline__ Top2<R> scan_row(const Params& p, const In* row, const R* __restrict__ Ps,
                                          int lane, int sub, int wpr) {
     const int M = (int)p.M;
@@ -881,17 +881,8 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 #ifndef ELA_MINB_ONE
 #define ELA_MINB_ONE 2
 #endif
-#ifndef ELA_UNROLL_ONE
-#define ELA_UNROLL_ONE 4
-#endif
 #define ELA_THREADS_MULTI 512
 #define ELA_MINB_MULTI 1
-#ifndef ELA_UNROLL_EXACT
-#define ELA_UNROLL_EXACT 4
-#endif
-#ifndef ELA_UNROLL_MULTI
-#define ELA_UNROLL_MULTI 4
-#endif
 #define ELA_MAX_S 256
 #define ELA_WS_HEADER 256
 
@@ -901,7 +892,7 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 //                   a round's bids go straight into the CTA's shared list.
 //   MULTI == true:  S CTAs share a problem; CTA c owns the block of rows
 //                   [c*rpc, (c+1)*rpc), rpc = ceil(N/S) (few TLB pages per CTA)
-template <typename In, typename R, bool MULTI, int THREADS, int MINB, int UNROLL>
+template <typename In, typename R, bool MULTI, int THREADS, int MINB>
 __global__ void __launch_bounds__(THREADS, MINB)
 auction_kernel(const Params p) {
     typedef Bits<R> BT;
@@ -999,7 +990,7 @@ auction_kernel(const Params p) {
                 const bool exact_ok = M >= ELA_SMALL_M;
                 // a row's bid from its complete top-2: tie re-scan, column, entry
                 auto emit = [&](int k, int q, const In* row, Top2<R> tt) {
-                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1);
+                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, P, lane, 0, 1);
                     if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                     int j1;
                     R bid;
@@ -1034,8 +1025,8 @@ auction_kernel(const Params p) {
                     Top2<R> tt;
                     top2_init(tt);
                     const bool exact_first = (wpr == 1) && s_exact;  // tie-heavy rows: one exact pass
-                    if (has) tt = exact_first ? scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1)
-                                              : scan_row_fast<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                    if (has) tt = exact_first ? scan_row<In, R>(p, row, P, lane, 0, 1)
+                                              : scan_row_fast<In, R>(p, row, P, lane, sub, wpr);
 #ifdef ELA_PROF
                     if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][8], (unsigned long long)(clock64() - pt1));
 #endif
@@ -1053,7 +1044,7 @@ auction_kernel(const Params p) {
                         if (__syncthreads_or(rowtie)) {  // also orders the wtop reads before rewrites
                             Top2<R> ex;
                             top2_init(ex);
-                            if (rowtie) ex = scan_row<In, R, UNROLL>(p, row, P, lane, sub, wpr);
+                            if (rowtie) ex = scan_row<In, R>(p, row, P, lane, sub, wpr);
                             if (rowtie && lane == 0) wtop[warp] = ex;
                             __syncthreads();
                             if (rowtie && sub == 0) {
@@ -1064,7 +1055,7 @@ auction_kernel(const Params p) {
                             }
                         }
                     } else if (exact_ok && has && tt.v1 == tt.v2 && !exact_first) {
-                        tt = scan_row<In, R, UNROLL>(p, row, P, lane, 0, 1);
+                        tt = scan_row<In, R>(p, row, P, lane, 0, 1);
                     }
                     if (has && sub == 0 && lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
 #ifdef ELA_PROF
@@ -1693,10 +1684,10 @@ auction_cluster_kernel(const Params p) {
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
                 if (s_exact) {  // tie-heavy rows: one exact pass
-                    tt = scan_row<In, R, ELA_UNROLL_EXACT>(p, row, P, lane, 0, 1);
+                    tt = scan_row<In, R>(p, row, P, lane, 0, 1);
                 } else {
-                    tt = scan_row_fast<In, R, ELA_UNROLL_MULTI>(p, row, P, lane, 0, 1);
-                    if (tt.v1 == tt.v2) tt = scan_row<In, R, ELA_UNROLL_EXACT>(p, row, P, lane, 0, 1);
+                    tt = scan_row_fast<In, R>(p, row, P, lane, 0, 1);
+                    if (tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, P, lane, 0, 1);
                 }
                 if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                 int j1;
@@ -2124,14 +2115,14 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
         return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
     if (pl.S == 1) {
-        auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, ELA_UNROLL_ONE>;
+        auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
         const int64_t grid = p.B < (1ll << 20) ? p.B : (1ll << 20);
         kern<<<(unsigned int)grid, ELA_THREADS_ONE, pl.smem, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
-    auto kern = auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI, ELA_UNROLL_MULTI>;
+    auto kern = auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
         return ELA_ERR_CUDA;
     int occ = 0;
