@@ -1464,17 +1464,25 @@ auction_cluster_kernel(const Params p) {
     }
     cluster.sync();               // every CTA of the cluster runs before any remote store
 
+#ifdef ELA_PROF
+    if (blockIdx.x == 0 && threadIdx.x == 0) { g_trace[8191][0] = clock64(); g_trace[8191][1] = globaltimer_ns(); }
+#endif
     for (int64_t b = team; b < p.B; b += p.ngroups) {
         const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
         for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; win[j] = 0; owner[j] = (IX)-1; }
         for (int i = tid; i < N; i += blockDim.x) rowcol[i] = (IX)-1;
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
+        R eps = (R)p.eps[0];  // this epsilon (read once per epsilon)
         __syncthreads();
         int K = compact_unassigned(rowcol, N, act, s_scan);  // rows that bid this round, ascending
         bool small = small_ok && K <= ELA_SMALL_ROUND;
+#ifdef ELA_PROF
+        long long lastS5 = 0;
+#endif
         while (ph < p.n_eps) {
             if (it == p.max_iter || K == 0) {  // this epsilon is done
+                PROF_MARK(E0);
                 if (small) {  // the cluster's next stores into its CTAs' bid lists wait for everyone
                     if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
                     cluster_arrive_release();
@@ -1514,18 +1522,26 @@ auction_cluster_kernel(const Params p) {
                     }
                 }
                 if (++ph >= p.n_eps) break;
+                eps = (R)p.eps[ph];
                 it = 0;
                 for (int j = tid; j < M; j += blockDim.x) owner[j] = (IX)-1;
                 for (int i = tid; i < N; i += blockDim.x) rowcol[i] = (IX)-1;
                 __syncthreads();
                 K = compact_unassigned(rowcol, N, act, s_scan);
                 small = small_ok && K <= ELA_SMALL_ROUND;
+#ifdef ELA_PROF
+                if (b == 0 && leader && rank == 0 && tid == 0) {
+                    atomicAdd(&g_prof[13], (unsigned long long)(clock64() - E0)); atomicAdd(&g_prof[14], 1ull);
+                }
+#endif
                 continue;
             }
-            const R eps = (R)p.eps[ph];
             if (small) {
                 if (!leader) { K = 0; continue; }  // wait at the end of the epsilon
                 PROF_MARK(S0);
+#ifdef ELA_PROF
+                if (b == 0 && rank == 0 && tid == 0 && lastS5) atomicAdd(&g_prof[12], (unsigned long long)(S0 - lastS5));
+#endif
                 if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }  // last round's data read everywhere
                 const int bp = ASYNC ? (int)(sr & 1) : 0;
                 Top2<R>* pb = part + (size_t)bp * CS * ELA_SMALL_ROUND;
@@ -1664,8 +1680,8 @@ auction_cluster_kernel(const Params p) {
                     atomicAdd(&g_prof[0], (unsigned long long)(S1 - S0)); atomicAdd(&g_prof[1], (unsigned long long)(S2 - S1));
                     atomicAdd(&g_prof[2], (unsigned long long)(S3 - S2)); atomicAdd(&g_prof[3], (unsigned long long)(S4 - S3));
                     atomicAdd(&g_prof[5], (unsigned long long)(S5 - S4)); atomicAdd(&g_prof[4], 1ull);
-                    atomicAdd(&g_prof[12], (unsigned long long)K);
                 }
+                lastS5 = clock64();
 #endif
                 K = s_cnt;
                 ++it;
@@ -1832,6 +1848,9 @@ auction_cluster_kernel(const Params p) {
             if (small_ok && K <= ELA_SMALL_ROUND) small = true;
             PROF_MARK(L4);
 #ifdef ELA_PROF
+            if (b == 0 && leader && rank == 0 && tid == 0 && nent < 513) {
+                atomicAdd(&g_prof[15], (unsigned long long)(L4 - L0)); 
+            }
             if (leader && rank == 0 && tid == 0 && nent >= 513) {
                 atomicAdd(&g_prof[6], (unsigned long long)(L1 - L0)); atomicAdd(&g_prof[7], (unsigned long long)(L2 - L1));
                 atomicAdd(&g_prof[8], (unsigned long long)(L3 - L2)); atomicAdd(&g_prof[9], (unsigned long long)(L4 - L3));
@@ -1872,6 +1891,9 @@ auction_cluster_kernel(const Params p) {
         }
         __syncthreads();
     }
+#ifdef ELA_PROF
+    if (blockIdx.x == 0 && threadIdx.x == 0) { g_trace[8191][2] = clock64(); g_trace[8191][3] = globaltimer_ns(); }
+#endif
     cluster.sync();  // no remote store may target a CTA that has exited
 }
 
