@@ -940,11 +940,13 @@ auction_kernel(const Params p) {
         for (int q = tid; q < my_rows; q += blockDim.x) { rowcol[q] = -1; rowbid[q] = -1; }
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
+        R eps = (R)p.eps[0];  // this epsilon (read once per epsilon)
         bool rebuild = true;  // the active list is rebuilt from rowcol at problem and epsilon starts
         __syncthreads();
         while (ph < p.n_eps) {
             if (it == p.max_iter) {  // round budget of this epsilon used up
                 if (++ph < p.n_eps) {  // the next epsilon starts from unassigned rows
+                    eps = (R)p.eps[ph];
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
                     for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
                 }
@@ -953,7 +955,6 @@ auction_kernel(const Params p) {
                 __syncthreads();
                 continue;
             }
-            const R eps = (R)p.eps[ph];
             const unsigned int t1 = t + 1;
             PROF_MARK(pt0);
             // ---- own rows that bid this round (otherwise listed by the last election)
@@ -1149,6 +1150,7 @@ auction_kernel(const Params p) {
             if (ntot == 0) {  // nobody bid: this epsilon's solve has converged
                 rebuild = true;
                 if (++ph < p.n_eps) {  // the next epsilon starts from unassigned rows
+                    eps = (R)p.eps[ph];
                     for (int q = tid; q < my_rows; q += blockDim.x) rowcol[q] = -1;
                     for (int j = tid; j < M; j += blockDim.x) owner[j] = -1;
                 }
