@@ -234,9 +234,10 @@ def main():
         stream and all enqueued before one synchronisation: the GPU runs ahead
         of the host (each L2 flush gives the host time to enqueue the next
         call), so the events bracket device work only, not host-side launch
-        latency.  Returns (list of ms, last result)."""
+        latency.  One extra leading call is run and not timed.  Returns (list of
+        the n timed ms, last result)."""
         evs, out = [], None
-        for _ in range(n):
+        for _ in range(n + 1):  # the first (untimed) iteration absorbs start-up after a barrier
             if flush_between:
                 flush.zero_()
             e0 = torch.cuda.Event(enable_timing=True)
@@ -246,7 +247,7 @@ def main():
             e1.record(stream)
             evs.append((e0, e1))
         torch.cuda.synchronize()
-        return [a.elapsed_time(b) for a, b in evs], out
+        return [a.elapsed_time(b) for a, b in evs[1:]], out
 
     sched = [1e-2] if args.fixed_eps else ela.workloads.CFG2_SCHEDULE
     cost_cpu = ela.workloads.cfg2()
