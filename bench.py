@@ -49,9 +49,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the bandwidth-bound config-5 leg")
-    ap.add_argument("--profile-case", choices=["cfg5-small"], default=None,
+    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4"], default=None,
                     help="run one small solve for an ncu capture and exit (cfg5-small: B=2 N=M=8192 "
-                         "bf16, 256 MB > L2, max_iter 50)")
+                         "bf16, 256 MB > L2, max_iter 50; cfg4: the B=256 N=M=512 batch, 256 MB)")
     ap.add_argument("--fixed-eps", action="store_true",
                     help="reference mode: constant epsilon 1e-2 instead of the cfg2 epsilon schedule")
     return ap.parse_args()
@@ -167,13 +167,16 @@ def profile_case(args):
     """One warm-up and one measured solve of a small case, for ncu captures."""
     import efficient_linear_assignment_b200 as ela
     torch.cuda.set_device(0)
-    c = ela.workloads.cfg5(8, 8192)[:2].contiguous().cuda()
+    if args.profile_case == "cfg4":
+        c, eps, mi, es = ela.workloads.cfg4().cuda(), [1e-2], 1000, 4
+    else:
+        c, eps, mi, es = ela.workloads.cfg5(8, 8192)[:2].contiguous().cuda(), [1.0 / 8193], 50, 2
     for _ in range(2):
-        r = ela.auction_solve(c, [1.0 / 8193], 50, ela.PATH_AUTO)
+        r = ela.auction_solve(c, eps, mi, ela.PATH_AUTO)
     torch.cuda.synchronize()
     ela._lib.check(int(r[3].item()), "profile case")
     print(json.dumps({"profile_case": args.profile_case, "row_bids": int(r[2][:, 1].sum().item()),
-                      "alg_bytes": int(r[2][:, 1].sum().item()) * 8192 * 2}))
+                      "alg_bytes": int(r[2][:, 1].sum().item()) * c.shape[2] * es}))
 
 
 def main():
