@@ -1,9 +1,9 @@
 """Record golden outputs by running the REFERENCE solver (not this project).
 
-Run in a checkout that has the reference project at $ELA_REFERENCE_SRC
-(default /root/reference/src):
+Point ELA_REFERENCE_SRC at the reference project's `src` directory (the one
+that holds the `efficient_linear_assignment` package) and run:
 
-    python tests/golden/make_golden.py
+    ELA_REFERENCE_SRC=<reference checkout>/src python tests/golden/make_golden.py
 
 For every case of cases.py it runs the reference's AuctionTorch.solve
 (src/efficient_linear_assignment/auction/torch_backend.py:9-159) on one CPU
@@ -25,7 +25,9 @@ import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(os.path.dirname(HERE)))
-sys.path.insert(0, os.environ.get("ELA_REFERENCE_SRC", "/root/reference/src"))
+if not os.environ.get("ELA_REFERENCE_SRC"):
+    sys.exit("set ELA_REFERENCE_SRC to the reference project's src directory")
+sys.path.insert(0, os.environ["ELA_REFERENCE_SRC"])
 sys.dont_write_bytecode = True
 
 from efficient_linear_assignment.auction import torch_backend as ref_tb  # noqa: E402
