@@ -4,13 +4,19 @@ Workload: B=1, N=M=4096 fp32 uniform[0,1) costs (seed 1),
 epsilon scaling 1.0 -> 1e-2 by 0.25 ([1, .25, .0625, .015625, .01]), max_iter
 1000 per epsilon.  One step = one full solve.  With --gpus N (one process per
 GPU under torchrun) every rank solves its own replica (a single problem does
-not split across GPUs).  Also reported, each on its own line key:
+not split across GPUs): `value` is then the per-solve latency, the max over
+ranks, not divided by N.  Also reported, each on its own line key:
   "fixed_eps": the same matrix with the reference's constant epsilon 1e-2;
+  "cfg1":      config 1 (B=4, N=M=128 fp32, eps 1e-2), replicas;
+  "cfg3":      config 3 (B=1, N=M=4096 fp16 and bf16, eps 1e-2), replicas;
   "batched":   config 4 (B=256, N=M=512, low-rank + noise) sharded over the
-               ranks (256/N problems each);
+               ranks (256/N problems each): solves/sec of the whole job;
   "cfg5":      config 5 (B=8, N=M=8192 bf16 integer costs, eps 1/8193,
                1000 rounds; the bandwidth-bound case) sharded 8/N per rank,
                with its own HBM roofline.
+The sharded legs gather their assignments after timing and check them: at
+N > 1 against a one-GPU solve of the whole batch on rank 0, at N = 1 (config
+4) against the CPU oracle.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
@@ -223,7 +229,7 @@ def main():
         ws = torch.empty((wsb,), dtype=torch.uint8, device=dev)
         e = (ctypes.c_double * len(eps))(*eps)
         argv = (cst.data_ptr(), code, B, N, M, cst.stride(0), cst.stride(1), e, len(eps), max_iter, ela.PATH_AUTO,
-                outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(), outs[3].data_ptr(), ws.data_ptr(), wsb,
+                ela.TIE_HIGHEST_ROW, outs[0].data_ptr(), outs[1].data_ptr(), outs[2].data_ptr(), outs[3].data_ptr(), ws.data_ptr(), wsb,
                 torch.cuda.current_stream(dev).cuda_stream)
 
         def run():
@@ -282,7 +288,7 @@ def main():
     ela._lib.check(int(status.item()), "timed solve")
     per_step = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     ms_step = max_over_ranks(sum(per_step) / len(per_step))
-    value = ms_step / world  # ms per solve over the whole job (one solve per rank per step)
+    value = ms_step  # per-solve latency: every rank solves its own replica, max over ranks
 
     # roofline of the solve kernel: algorithmic cost bytes (row-bids x M x 4 B) per launch
     peak, peak_kind = measured_peak_hbm()
@@ -320,7 +326,51 @@ def main():
         torch.cuda.synchronize()
         if k >= args.warmup:
             e2e_ms.append(e0.elapsed_time(e1))
-    e2e_val = max_over_ranks(statistics.mean(e2e_ms)) / world if e2e_ms else None
+    e2e_val = max_over_ranks(statistics.mean(e2e_ms)) if e2e_ms else None
+
+    def gather_and_check(local_assign, B, full_cost, eps, max_iter, oracle_at_n1=False):
+        """All-gather the sharded (B_r, N) assignments; rank 0 compares them with
+        a one-GPU solve of the whole batch (N > 1) or with the CPU oracle (N = 1,
+        when asked).  Runs after the timed region."""
+        from efficient_linear_assignment_b200.sharding import gather_assignments
+        full = gather_assignments(local_assign, B) if world > 1 else local_assign
+        if rank != 0:
+            return None
+        if world > 1:
+            ref, _, _ = ela.solve(full_cost.to(dev), eps, max_iter)
+            against = "one-GPU solve of the whole batch on rank 0"
+            equal = bool(torch.equal(full.to(dev), ref))
+        elif oracle_at_n1:
+            from oracle import oracle
+            ref, _, _ = oracle.solve(full_cost, eps, max_iter, nthreads=os.cpu_count() or 1)
+            against = "CPU oracle (C restatement of the reference)"
+            equal = bool(torch.equal(full.cpu(), ref))
+        else:
+            return None
+        return {"against": against, "equal": equal, "rows": int(full.numel())}
+
+    def replica_leg(name, cst, eps, es, workload):
+        """ms per step of one batch solved by every rank (replicas), with the
+        roofline of its algorithmic bytes (row-bids x M x element size)."""
+        fn = prepared(cst.to(dev), eps, 1000)
+        for _ in range(args.warmup):
+            r = fn()
+        ms, r = timed(fn, args.steps)
+        ela._lib.check(int(r[3].item()), name)
+        m = max_over_ranks(statistics.mean(ms))
+        bids = int(r[2][:, 1].sum().item())
+        alg = bids * cst.shape[2] * es
+        ach = alg / (m * 1e-3) / 1e9
+        return {"workload": workload, "ms_per_step": round(m, 4), "solves_per_sec": round(cst.shape[0] / (m * 1e-3), 2),
+                "rounds": int(r[2][:, 0].max().item()), "row_bids": bids,
+                "roofline": {"bound": "hbm", "achieved": round(ach, 2), "peak": peak, "unit": "GB/s",
+                             "frac": round(ach / peak, 5), "alg_bytes_per_launch": alg}}
+
+    cfg1 = replica_leg("cfg1 solve", ela.workloads.cfg1(), [1e-2], 4,
+                       "cfg1: B=4 N=M=128 fp32 uniform (seed 0), eps 1e-2, max_iter 1000")
+    cfg3 = {dt: replica_leg(f"cfg3 {dt} solve", ela.workloads.cfg3(getattr(torch, dt)), [1e-2], 2,
+                            f"cfg3: B=1 N=M=4096 {dt} uniform (seed 2), fp32 prices, eps 1e-2, max_iter 1000")
+            for dt in ("float16", "bfloat16")}
 
     # batched config 4, sharded over the ranks
     batched = None
@@ -329,7 +379,8 @@ def main():
         from efficient_linear_assignment_b200.sharding import shard_range
         lo, hi = shard_range(B4, world, rank)
         per = hi - lo
-        c4 = ela.workloads.cfg4()[lo:hi].contiguous().to(dev)
+        c4_all = ela.workloads.cfg4()
+        c4 = c4_all[lo:hi].contiguous().to(dev)
         solve4 = prepared(c4, [1e-2], 1000)
         for _ in range(args.warmup):
             r4 = solve4()
@@ -341,7 +392,11 @@ def main():
         bm = max_over_ranks(statistics.mean(b_ms))
         batched = {"workload": "cfg4: B=256 N=M=512 fp32 low-rank+noise, eps 1e-2", "problems_per_gpu": per,
                    "ms_per_step": round(bm, 4), "value": round(B4 / (bm * 1e-3), 2), "unit": "solves/sec",
-                   "scaling": "strong", "ms_min": round(min(b_ms), 4), "ms_median": round(statistics.median(b_ms), 4)}
+                   "scaling": "strong", "ms_min": round(min(b_ms), 4), "ms_median": round(statistics.median(b_ms), 4),
+                   "ms_steps_rank0": [round(x, 4) for x in b_ms],
+                   "row_bids_per_gpu": int(r4[2][:, 1].sum().item()),
+                   "max_rounds": int(r4[2][:, 0].max().item())}
+        batched["verified"] = gather_and_check(r4[0].clone(), B4, c4_all, [1e-2], 1000, oracle_at_n1=True)
 
     # the reference's own mode on the cfg2 matrix: constant epsilon 1e-2
     fixed = None
@@ -362,7 +417,8 @@ def main():
         from efficient_linear_assignment_b200.sharding import shard_range
         B5, N5 = 8, 8192
         lo, hi = shard_range(B5, world, rank)
-        c5 = ela.workloads.cfg5(B5, N5)[lo:hi].contiguous().to(dev)
+        c5_all = ela.workloads.cfg5(B5, N5)
+        c5 = c5_all[lo:hi].contiguous().to(dev)
         eps5 = [1.0 / (N5 + 1)]
         solve5 = prepared(c5, eps5, 1000)
         r5 = solve5()
@@ -387,6 +443,8 @@ def main():
                 "roofline": {"bound": "hbm", "achieved": round(ach5, 1), "peak": peak, "unit": "GB/s",
                              "frac": round(ach5 / peak / world, 4), "alg_bytes_per_step": int(alg5),
                              "note": "frac per GPU: achieved / (peak x GPUs)"}}
+        del solve5
+        cfg5["verified"] = gather_and_check(r5[0].clone(), B5, c5_all, eps5, 1000)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -403,7 +461,8 @@ def main():
             "data": "synthetic (seeded uniform[0,1), seed 1; cfg4 seed 3; cfg5 seed 4)",
             "config": {"workload": ("cfg2 (fixed eps 1e-2): B=1 N=M=4096 fp32, max_iter 1000" if args.fixed_eps else
                                     "cfg2: B=1 N=M=4096 fp32, eps 1.0->1e-2 x0.25, max_iter 1000/eps"),
-                       "parallelism": f"replicas x{world}", "l2": "flushed (256 MB write) between steps",
+                       "parallelism": f"replicas x{world} (value = per-solve latency, max over ranks)",
+                       "l2": "flushed (256 MB write) between steps",
                        "rounds": rounds, "row_bids": row_bids,
                        "us_per_round": round(ms_step * 1e3 / max(rounds, 1), 3)},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -415,6 +474,8 @@ def main():
                     "h2d_bytes_per_step": cost_cpu.numel() * 4, "d2h_bytes_per_step": N_MAIN * 8},
             "gpu_launches": args.steps,
             "fixed_eps": fixed,
+            "cfg1": cfg1,
+            "cfg3": cfg3,
             "round1": round1,
             "batched": batched,
             "cfg5": cfg5,

@@ -19,6 +19,7 @@ ELA_ERR_UNSUPPORTED = 4
 ELA_ERR_INTERNAL = 5
 
 PATH_AUTO, PATH_CTA, PATH_GRID, PATH_CLUSTER = 0, 1, 2, 3
+TIE_HIGHEST_ROW, TIE_LOWEST_ROW = 0, 1  # ELA_TIE_*: election rule among bids within 1e-5
 
 # Every symbol include/ela_auction.h declares, with (restype, argtypes).
 _c = ctypes
@@ -28,11 +29,11 @@ SIGNATURES = {
     "ela_auction_workspace_bytes": (_c.c_size_t, [_c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int]),
     "ela_auction_solve": (_c.c_int, [
         _c.c_void_p, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64,
-        _c.POINTER(_c.c_double), _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p,
+        _c.POINTER(_c.c_double), _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p,
         _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t, _c.c_void_p]),
     "ela_auction_solve_noalloc": (_c.c_int, [
         _c.c_void_p, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64,
-        _c.POINTER(_c.c_double), _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p,
+        _c.POINTER(_c.c_double), _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p,
         _c.c_void_p, _c.c_void_p, _c.c_void_p]),
     "ela_auction_set_wait_limit_ns": (None, [_c.c_uint64]),
     "ela_auction_debug_skip_arrive": (None, [_c.c_int]),

@@ -92,12 +92,16 @@ def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[
 
     auto_pad=True accepts any N and M and returns what solving
     ``pad_input(cost)`` and keeping the real rows (``unpad_result``) returns.
-    When M needs padding and there are no more dummy rows than dummy columns,
-    the problem is solved as given, without the copy: the dummy columns (cost
-    1e9 for real rows) never enter a real row's top-2 bid, and the dummy rows
-    (cost 0 on dummy columns, 1e9 on real ones) settle on dummy columns, so
-    the real rows' rounds are the same.  Otherwise the reference's dummy rows
-    can bid on real columns, and the padded copy is solved.
+    When M needs padding, M >= 128 and there are no more dummy rows than
+    dummy columns, the problem is solved as given, without the copy: the
+    dummy columns (cost 1e9 for real rows) never enter a real row's top-2 bid
+    nor its tie choice (for rows of 128 or more columns torch.topk's tied
+    column is fixed by the first two occurrences of the maximum), and the
+    dummy rows (cost 0 on dummy columns, 1e9 on real ones) settle on dummy
+    columns, so the real rows' rounds are the same.  Below 128 columns the
+    tied column comes from an introselect over the whole row, whose steps
+    depend on the row length, and with more dummy rows than dummy columns the
+    dummy rows bid on real columns: both solve the padded copy.
     """
     is_batched = cost_matrix.ndim == 3
     if not is_batched:
@@ -106,7 +110,7 @@ def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[
     if auto_pad and (N % 8 != 0 or M % 8 != 0):
         from .utils import get_pad_size, pad_input, unpad_result
         pn, pm = get_pad_size(N), get_pad_size(M)
-        if pm == 0 or pn > pm or M < 2:  # dummy rows could reach real columns: solve the copy
+        if pm == 0 or pn > pm or M < 128:  # the padding could change a bid or a tie: solve the copy
             padded, shape = pad_input(cost_matrix)
             out = linear_assignment(padded, epsilon, max_iter, backend, return_indices)
             out = unpad_result(out, shape) if return_indices else out[:, :N, :M]

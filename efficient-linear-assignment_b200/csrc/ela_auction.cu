@@ -77,6 +77,12 @@ template <> struct Bits<double> {
     static __device__ __forceinline__ double from(U u) { return __longlong_as_double((long long)u); }
 };
 
+// Election key of a row among the bids within 1e-5 of a column's new price;
+// the largest key wins (atomicMax), 0 means no winner.  ELA_TIE_HIGHEST_ROW is
+// the reference's rule (index_put_ with ascending rows keeps the last writer,
+// torch_backend.py:126-136); ELA_TIE_LOWEST_ROW keeps the first.
+__device__ __forceinline__ int win_key(int row, int N, int rule) { return rule == ELA_TIE_LOWEST_ROW ? N - row : row + 1; }
+
 // ------------------------------------------------------------- cost loading
 template <typename In> struct Elem;
 template <> struct Elem<float> {
@@ -370,6 +376,7 @@ struct Params {
     int skip_publish;        // test hook: CTA 0 never publishes its first round
     int max_wpr;             // most warps that share one row's scan (power of two)
     int team;                // cluster path: clusters per problem
+    int tie_rule;            // ELA_TIE_*: which row wins among bids within 1e-5 of the new price
     size_t team_bytes;       // cluster path: workspace bytes per team
 };
 
@@ -1172,13 +1179,13 @@ auction_kernel(const Params p) {
                     const int i = valid ? lrow[lane] : 0;  // row0 == 0 on this path
                     if (valid) atomicMax(&maxb[j], BT::to(lbid[lane]));
                     __syncwarp();
-                    if (valid && absval(sub_rn(lbid[lane], BT::from(maxb[j]))) < tol) atomicMax(&win[j], i + 1);
+                    if (valid && absval(sub_rn(lbid[lane], BT::from(maxb[j]))) < tol) atomicMax(&win[j], win_key(i, N, p.tie_rule));
                     __syncwarp();
                     int nxt = -1;  // this entry's bidder in the next round
                     if (valid) {
                         nxt = i;  // lost: bids again
                         rowbid[i] = -1;
-                        if (win[j] == i + 1) {
+                        if (win[j] == win_key(i, N, p.tie_rule)) {
                             const int prev = owner[j];
                             if (prev >= 0) rowcol[prev] = -1;
                             owner[j] = i;
@@ -1201,14 +1208,14 @@ auction_kernel(const Params p) {
                 __syncthreads();
                 for (int e = tid; e < ntot; e += blockDim.x) {
                     const int j = lcol[e];
-                    if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], lrow[e] + 1);
+                    if (absval(sub_rn(lbid[e], BT::from(maxb[j]))) < tol) atomicMax(&win[j], win_key(lrow[e], N, p.tie_rule));
                 }
                 __syncthreads();
                 for (int q = tid; q < my_rows; q += blockDim.x) {
                     const int jb = rowbid[q];
                     int col = rowcol[q];
                     if (jb >= 0) {
-                        col = (win[jb] == row0 + q + 1) ? jb : -1;
+                        col = (win[jb] == win_key(row0 + q, N, p.tie_rule)) ? jb : -1;
                         if (!MULTI && col >= 0) owner[col] = q;
                         rowbid[q] = -1;
                     } else if (col >= 0 && maxb[col] != 0) {
@@ -1346,8 +1353,10 @@ __device__ __forceinline__ void mbar_init(unsigned long long* mb, unsigned int c
 __device__ __forceinline__ void mbar_expect_tx(unsigned long long* mb, unsigned int bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(mb)), "r"(bytes) : "memory");
 }
-// Bounded wait for phase `parity` of a local mbarrier; false on timeout.
-__device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int parity, unsigned long long limit_ns) {
+// Bounded wait for phase `parity` of a local mbarrier; false on timeout or
+// when *abort (the cluster's failure mark) is set.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int parity, unsigned long long limit_ns,
+                                          const volatile int* abort) {
     const unsigned int a = smem_addr(mb);
     const unsigned long long t0 = globaltimer_ns();
     for (;;) {
@@ -1355,6 +1364,7 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int p
         asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                      : "=r"(done) : "r"(a), "r"(parity) : "memory");
         if (done) return true;
+        if (*abort) return false;
         if (globaltimer_ns() - t0 > limit_ns) return false;
     }
 }
@@ -1412,6 +1422,7 @@ auction_cluster_kernel(const Params p) {
     __shared__ int s_segcnt[ELA_MAX_S];
     __shared__ int s_exoff[ELA_MAX_S + 1];
     __shared__ __align__(8) unsigned long long s_mbar[2];  // small-round partials, by round parity
+    __shared__ int s_abort;  // some CTA of this cluster failed (set locally or by a peer through DSMEM)
     // fp32 partials are 16 bytes: one asynchronous store per destination CTA
     constexpr bool ASYNC = (sizeof(Top2<R>) == 16);
 
@@ -1460,11 +1471,31 @@ auction_cluster_kernel(const Params p) {
     if (tid == 0) {
         s_ties = 0;
         s_exact = 0;
+        s_abort = 0;
         mbar_init(&s_mbar[0], 1);
         mbar_init(&s_mbar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     cluster.sync();               // every CTA of the cluster runs before any remote store
+
+    // ---- failure exit, taken by the whole cluster together.  A CTA leaves
+    // only through a cluster barrier phase that every other resident CTA must
+    // also arrive at, so until it arrives every peer is still resident: a CTA
+    // that fails by itself first marks s_abort in every CTA of the cluster
+    // (distributed shared memory), then arrives and waits.  Every CTA checks
+    // its own s_abort after each cluster barrier wait of the round loop (a
+    // failing peer's mark is released before its arrival) and then leaves the
+    // same way without storing to peers, since a failed peer may have exited.
+    // Waits count only resident CTAs, so the last leavers do not block.
+    auto leave = [&]() {
+        if (tid == 0) atomicExch(abort_flag, 1);
+        if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
+        if (tid < CS && !*(volatile int*)&s_abort) *cluster.map_shared_rank(&s_abort, tid) = 1;
+        cluster_arrive_release();
+        cluster_wait_acquire();
+    };
+    // (read once per CTA: every thread of the CTA must take the same way)
+#define ELA_CLUSTER_ABORT_CHECK() do { if (__syncthreads_or(*(volatile int*)&s_abort)) { leave(); return; } } while (0)
 
 #ifdef ELA_PROF
     if (blockIdx.x == 0 && threadIdx.x == 0) { g_trace[8191][0] = clock64(); g_trace[8191][1] = globaltimer_ns(); }
@@ -1486,9 +1517,10 @@ auction_cluster_kernel(const Params p) {
             if (it == p.max_iter || K == 0) {  // this epsilon is done
                 PROF_MARK(E0);
                 if (small) {  // the cluster's next stores into its CTAs' bid lists wait for everyone
-                    if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
+                    if (cl_pending) { cluster_wait_acquire(); cl_pending = false; ELA_CLUSTER_ABORT_CHECK(); }
                     cluster_arrive_release();
                     cluster_wait_acquire();
+                    ELA_CLUSTER_ABORT_CHECK();
                 }
                 if (small && TC > 1) {
                     // the leader publishes its prices; the other clusters wait for them
@@ -1519,7 +1551,7 @@ auction_cluster_kernel(const Params p) {
                             s_fail = !ok;
                         }
                         __syncthreads();
-                        if (s_fail) { if (cl_pending) cluster_wait_acquire(); cluster.sync(); return; }
+                        if (s_fail) { leave(); return; }
                         for (int j = tid; j < M; j += blockDim.x) P[j] = __ldcg(pbuf + j);
                     }
                 }
@@ -1544,7 +1576,11 @@ auction_cluster_kernel(const Params p) {
 #ifdef ELA_PROF
                 if (b == 0 && rank == 0 && tid == 0 && lastS5) atomicAdd(&g_prof[12], (unsigned long long)(S0 - lastS5));
 #endif
-                if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }  // last round's data read everywhere
+                if (cl_pending) {  // last round's data read everywhere
+                    cluster_wait_acquire();
+                    cl_pending = false;
+                    ELA_CLUSTER_ABORT_CHECK();
+                }
                 const int bp = ASYNC ? (int)(sr & 1) : 0;
                 Top2<R>* pb = part + (size_t)bp * CS * ELA_SMALL_ROUND;
                 if (ASYNC && tid == 0)
@@ -1576,17 +1612,18 @@ auction_cluster_kernel(const Params p) {
                 }
                 PROF_MARK(S1);
                 if (ASYNC) {
-                    if (tid == 0) s_fail = !mbar_wait(&s_mbar[bp], (sr >> 1) & 1u, p.wait_ns);
+                    if (tid == 0) s_fail = !mbar_wait(&s_mbar[bp], (sr >> 1) & 1u, p.wait_ns, &s_abort);
                     __syncthreads();
                     if (s_fail) {
-                        atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
-                        cluster.sync();
+                        if (tid == 0 && !*(volatile int*)&s_abort) atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
+                        leave();
                         return;
                     }
                     ++sr;
                 } else {
                     cluster_arrive_release();
                     cluster_wait_acquire();
+                    ELA_CLUSTER_ABORT_CHECK();
                 }
                 PROF_MARK(S2);
                 // ---- each row's CS partials merged by one warp: column and bid
@@ -1618,13 +1655,13 @@ auction_cluster_kernel(const Params p) {
                         const int j = valid ? (int)lcol[lane] : 0;
                         if (valid) atomicMax(&Pbits[j], BT::to(lbid[lane]));
                         __syncwarp();
-                        if (valid && absval(sub_rn(lbid[lane], P[j])) < tol) atomicMax(&win[j], (int)lrow[lane] + 1);
+                        if (valid && absval(sub_rn(lbid[lane], P[j])) < tol) atomicMax(&win[j], win_key((int)lrow[lane], N, p.tie_rule));
                         __syncwarp();
                         int nxt = -1;  // this entry's bidder in the next round
                         if (valid) {
                             const int i = lrow[lane];
                             nxt = i;  // lost: bids again
-                            if (win[j] == i + 1) {
+                            if (win[j] == win_key(i, N, p.tie_rule)) {
                                 const int prev = owner[j];
                                 if (prev >= 0) rowcol[prev] = (IX)-1;
                                 owner[j] = (IX)i;
@@ -1643,13 +1680,13 @@ auction_cluster_kernel(const Params p) {
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) {
                         const int j = lcol[e];
-                        if (absval(sub_rn(lbid[e], P[j])) < tol) atomicMax(&win[j], (int)lrow[e] + 1);
+                        if (absval(sub_rn(lbid[e], P[j])) < tol) atomicMax(&win[j], win_key((int)lrow[e], N, p.tie_rule));
                     }
                     __syncthreads();
                     for (int e = tid; e < K; e += blockDim.x) {
                         const int j = lcol[e], i = lrow[e];
                         int ev = -2;
-                        if (win[j] == i + 1) {
+                        if (win[j] == win_key(i, N, p.tie_rule)) {
                             const int prev = owner[j];
                             if (prev >= 0) rowcol[prev] = (IX)-1;
                             owner[j] = (IX)i;
@@ -1723,7 +1760,7 @@ auction_cluster_kernel(const Params p) {
             bool compact;  // entries at 0..nent-1 (else slots rank*rpc + k)
             if (TC == 1) {
                 // ---- exchange through distributed shared memory
-                if (cl_pending) cluster_wait_acquire();
+                if (cl_pending) { cluster_wait_acquire(); cl_pending = false; ELA_CLUSTER_ABORT_CHECK(); }
                 __syncthreads();
                 for (int e = tid; e < Kl * CS; e += blockDim.x) {
                     const int k = e / CS, dst = e % CS;
@@ -1736,6 +1773,7 @@ auction_cluster_kernel(const Params p) {
                 if (tid < CS) cluster.map_shared_rank(cnt, tid)[rank] = Kl;
                 cluster_arrive_release();
                 cluster_wait_acquire();
+                ELA_CLUSTER_ABORT_CHECK();
                 if (tid == 0) {
                     int acc = 0;
                     for (int r = 0; r < CS; ++r) { s_off[r] = acc; acc += cnt[r]; }
@@ -1795,12 +1833,11 @@ auction_cluster_kernel(const Params p) {
                     }
                 }
                 __syncthreads();
-                if (s_fail) { if (cl_pending) cluster_wait_acquire(); cluster.sync(); return; }
+                if (s_fail) { leave(); return; }
                 if (s_extra && !read_extra_entries<R, IX>(tb + (size_t)((t & 1) * ST) * p.seg_bytes, p.seg_bytes, ST,
                                                           s_segcnt, s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag,
                                                           p.status)) {
-                    if (cl_pending) cluster_wait_acquire();
-                    cluster.sync();
+                    leave();
                     return;
                 }
                 nent = s_total;
@@ -1827,13 +1864,13 @@ auction_cluster_kernel(const Params p) {
             for (int e = tid; e < nent; e += blockDim.x) {
                 const int sl = slot_of(e);
                 const int j = lcol[sl];
-                if (absval(sub_rn(lbid[sl], P[j])) < tol) atomicMax(&win[j], (int)lrow[sl] + 1);
+                if (absval(sub_rn(lbid[sl], P[j])) < tol) atomicMax(&win[j], win_key((int)lrow[sl], N, p.tie_rule));
             }
             __syncthreads();
             for (int e = tid; e < nent; e += blockDim.x) {
                 const int sl = slot_of(e);
                 const int j = lcol[sl], i = lrow[sl];
-                if (win[j] == i + 1) {
+                if (win[j] == win_key(i, N, p.tie_rule)) {
                     const int prev = owner[j];
                     if (prev >= 0) rowcol[prev] = (IX)-1;
                     owner[j] = (IX)i;
@@ -1867,9 +1904,10 @@ auction_cluster_kernel(const Params p) {
         }
         // ---- outputs of problem b (CTA 0 of the leader cluster); every CTA of
         //      the cluster is done with this problem's shared data
-        if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
+        if (cl_pending) { cluster_wait_acquire(); cl_pending = false; ELA_CLUSTER_ABORT_CHECK(); }
         cluster_arrive_release();
         cluster_wait_acquire();
+        ELA_CLUSTER_ABORT_CHECK();
         __syncthreads();
         if (leader && rank == 0) {
             int un = 0;
@@ -1897,6 +1935,7 @@ auction_cluster_kernel(const Params p) {
     if (blockIdx.x == 0 && threadIdx.x == 0) { g_trace[8191][2] = clock64(); g_trace[8191][3] = globaltimer_ns(); }
 #endif
     cluster.sync();  // no remote store may target a CTA that has exited
+#undef ELA_CLUSTER_ABORT_CHECK
 }
 
 }  // namespace
@@ -2124,19 +2163,39 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
             return ELA_ERR_CUDA;
         cudaLaunchConfig_t cfg = {};
-        cudaLaunchAttribute attr[1];
+        cudaLaunchAttribute attr[2];
         attr[0].id = cudaLaunchAttributeClusterDimension;
         attr[0].val.clusterDim.x = pl.cs; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+        attr[1].id = cudaLaunchAttributeCooperative;
+        attr[1].val.cooperative = 1;
         cfg.gridDim = dim3(pl.cs * pl.nclusters);
         cfg.blockDim = dim3(ELA_THREADS_MULTI);
         cfg.dynamicSmemBytes = pl.smem;
         cfg.stream = stream;
         cfg.attrs = attr;
-        cfg.numAttrs = 1;
-        // The launch never exceeds the clusters that fit at once (occupancy
-        // query), so the clusters of a team, which wait on one another, are
-        // co-resident; every such wait is also bounded.
-        return cudaLaunchKernelEx(&cfg, kern, p) == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
+        // The clusters of a team wait on one another (bounded waits), so they
+        // must be resident at once.  The launch never exceeds the clusters the
+        // occupancy query says fit, but other work on the GPU can hold SMs: a
+        // cooperative launch makes the driver refuse a grid it cannot
+        // co-schedule, and a refused team plan falls back to one cluster per
+        // problem (no inter-cluster waits; same results).
+        cfg.numAttrs = pl.team > 1 ? 2 : 1;
+        cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+        if (e != cudaSuccess && pl.team > 1) {
+            cudaGetLastError();  // the refused launch left no work behind
+            if (getenv("ELA_DEBUG_PLAN"))
+                fprintf(stderr, "ela plan: cooperative team launch refused (%s); one cluster per problem\n",
+                        cudaGetErrorString(e));
+            Params q = p;
+            q.team = 1;
+            q.team_bytes = 0;
+            q.ngroups = (int)(p.B < pl.ngroups * (int64_t)pl.team ? p.B : pl.ngroups * (int64_t)pl.team);
+            q.S = pl.cs;
+            cfg.gridDim = dim3(pl.cs * q.ngroups);
+            cfg.numAttrs = 1;
+            e = cudaLaunchKernelEx(&cfg, kern, q);
+        }
+        return e == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
     if (pl.S == 1) {
         auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE>;
@@ -2165,10 +2224,11 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
 // Validates the arguments common to the solve entry points and fills Params
 // (everything except the workspace pointers).
 int fill_params(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, int64_t stride_b,
-                int64_t stride_n, const double* eps_schedule, int n_eps, int max_iter,
+                int64_t stride_n, const double* eps_schedule, int n_eps, int max_iter, int tie_rule,
                 int64_t* assign_out, void* prices_out, int64_t* stats_out, Params& p) {
     const int es = elem_size(dtype);
     if (!cost || !assign_out || !prices_out) return ELA_ERR_ARGUMENT;
+    if (tie_rule != ELA_TIE_HIGHEST_ROW && tie_rule != ELA_TIE_LOWEST_ROW) return ELA_ERR_ARGUMENT;
     if (stride_n < M || (B > 1 && stride_b < (N - 1) * stride_n + M)) return ELA_ERR_ARGUMENT;
     memset(&p, 0, sizeof(p));
     p.cost = cost;
@@ -2176,6 +2236,7 @@ int fill_params(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, in
     for (int k = 0; k < n_eps; ++k) p.eps[k] = eps_schedule[k];
     p.n_eps = n_eps;
     p.max_iter = max_iter;
+    p.tie_rule = tie_rule;
     p.vec_ok = ((reinterpret_cast<uintptr_t>(cost) & 15u) == 0) && ((stride_n * es) % 16 == 0) &&
                ((stride_b * es) % 16 == 0) && ((M * es) % 16 == 0);
     p.assign_out = assign_out;
@@ -2229,21 +2290,46 @@ int dispatch(int dtype, const Params& p, const Plan& pl, cudaStream_t s) {
 // cudaGetSymbolAddress, looked up once per device.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[ELA_NOALLOC_SCRATCH_BYTES];
 
-#define ELA_MAX_DEVICES 64
+// The address is a property of the context that loaded the module: it is
+// cached per (device, current context), so a context replaced by
+// cudaDeviceReset (or a non-primary context made current by the caller) gets
+// its own lookup instead of a stale address.  cuCtxGetCurrent is reached
+// through the runtime's driver entry point, so the library does not link
+// libcuda.
+typedef int (*ela_ctx_get_current_fn)(void**);
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[ELA_MAX_DEVICES] = {nullptr};
+struct NoallocSlot { int dev; void* ctx; void* ptr; };
+#define ELA_NOALLOC_SLOTS 64
+NoallocSlot g_noalloc_slots[ELA_NOALLOC_SLOTS];
+int g_noalloc_used = 0;
+ela_ctx_get_current_fn g_ctx_get_current = nullptr;
 
 int noalloc_scratch(void** out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ELA_ERR_CUDA;
-    if (dev < 0 || dev >= ELA_MAX_DEVICES) return ELA_ERR_UNSUPPORTED;
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_ptr[dev] == nullptr) {
+    if (g_ctx_get_current == nullptr) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess || fn == nullptr)
+            return ELA_ERR_CUDA;
+        g_ctx_get_current = reinterpret_cast<ela_ctx_get_current_fn>(fn);
+    }
+    void* ctx = nullptr;
+    if (g_ctx_get_current(&ctx) != 0) return ELA_ERR_CUDA;
+    if (ctx == nullptr) {  // no context current on this thread yet: the lookup makes the primary one current
         void* ptr = nullptr;
         if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return ELA_ERR_CUDA;
-        g_noalloc_ptr[dev] = ptr;
+        if (g_ctx_get_current(&ctx) != 0 || ctx == nullptr) return ELA_ERR_CUDA;
     }
-    *out = g_noalloc_ptr[dev];
+    for (int k = 0; k < g_noalloc_used; ++k)
+        if (g_noalloc_slots[k].dev == dev && g_noalloc_slots[k].ctx == ctx) { *out = g_noalloc_slots[k].ptr; return ELA_OK; }
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return ELA_ERR_CUDA;
+    if (g_noalloc_used == ELA_NOALLOC_SLOTS) g_noalloc_used = 0;  // forget the oldest contexts
+    g_noalloc_slots[g_noalloc_used++] = NoallocSlot{dev, ctx, ptr};
+    *out = ptr;
     return ELA_OK;
 }
 
@@ -2251,7 +2337,7 @@ int noalloc_scratch(void** out) {
 
 extern "C" {
 
-int ela_auction_version(void) { return 100; }
+int ela_auction_version(void) { return 200; }
 
 const char* ela_status_string(int status) {
     switch (status) {
@@ -2282,7 +2368,7 @@ void ela_auction_debug_skip_arrive(int on) { g_skip_publish = on ? 1 : 0; }
 
 int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
                       int64_t stride_b, int64_t stride_n, const double* eps_schedule,
-                      int n_eps, int max_iter, int path, int64_t* assign_out,
+                      int n_eps, int max_iter, int path, int tie_rule, int64_t* assign_out,
                       void* prices_out, int64_t* stats_out, int32_t* status_out,
                       void* workspace, size_t workspace_bytes, void* stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
@@ -2291,8 +2377,8 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
     if (rc != ELA_OK || done) return rc;
     if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return ELA_ERR_ARGUMENT;
     Params p;
-    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, assign_out,
-                     prices_out, stats_out, p);
+    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, tie_rule,
+                     assign_out, prices_out, stats_out, p);
     if (rc != ELA_OK) return rc;
     Plan pl = {};
     rc = make_plan(dtype, B, N, M, path, pl, p.vec_ok != 0);
@@ -2318,15 +2404,16 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
 // instead of a caller-supplied workspace; see include/ela_auction.h.
 int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
                               int64_t stride_b, int64_t stride_n, const double* eps_schedule,
-                              int n_eps, int max_iter, int path, int64_t* assign_out,
-                              void* prices_out, int64_t* stats_out, int32_t* status_out, void* stream) {
+                              int n_eps, int max_iter, int path, int tie_rule,
+                              int64_t* assign_out, void* prices_out, int64_t* stats_out,
+                              int32_t* status_out, void* stream) {
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     bool done = false;
     int rc = check_common(dtype, B, N, M, eps_schedule, n_eps, max_iter, prices_out, stats_out, status_out, s, &done);
     if (rc != ELA_OK || done) return rc;
     Params p;
-    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, assign_out,
-                     prices_out, stats_out, p);
+    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, tie_rule,
+                     assign_out, prices_out, stats_out, p);
     if (rc != ELA_OK) return rc;
     Plan pl = {};
     rc = make_plan(dtype, B, N, M, path, pl, p.vec_ok != 0);

@@ -9,8 +9,9 @@ the solve path.  Two ways to drive it:
   ``gather_assignments`` collects the (B_r, N) results on every rank
   (one all-gather of int64 indices after the solve, outside the solve);
 * one process, several devices: ``solve_multi_device`` scatters the batch,
-  launches every slice on its device's current stream and gathers the
-  results onto the input's device.
+  launches every slice on its device's current stream without waiting, and
+  gathers the results onto the input's device (device status checked after
+  the gather).
 """
 from __future__ import annotations
 
@@ -46,10 +47,16 @@ def gather_assignments(local: torch.Tensor, B: int, group=None) -> torch.Tensor:
 
 
 def solve_multi_device(cost: torch.Tensor, devices: Sequence[torch.device],
-                       solve_fn: Callable[[torch.Tensor], tuple[torch.Tensor, torch.Tensor]]):
+                       solve_fn: Callable[[torch.Tensor], tuple] | None = None, *,
+                       epsilon=1e-2, max_iter: int = 1000):
     """Solve a (B,N,M) batch split over `devices` from one process.
 
-    solve_fn(cost_slice_on_device) -> (assignment, prices).  Returns the full
+    Default: every slice is copied to its device and its solve enqueued there
+    without waiting (no status read between devices), so the GPUs run at the
+    same time; the device status words are checked once, after the gather,
+    and a device-side error raises AuctionError.  ``solve_fn(cost_slice)`` ->
+    (assignment, prices[, status]) replaces the solve (it should not
+    synchronise if the devices are to overlap).  Returns the full
     (assignment, prices) on cost's device.
     """
     B = cost.shape[0]
@@ -59,7 +66,15 @@ def solve_multi_device(cost: torch.Tensor, devices: Sequence[torch.device],
         if a == b:
             continue
         part = cost[a:b].to(dev, non_blocking=True)
-        outs.append(solve_fn(part))
+        if solve_fn is None:
+            from .solver import solve
+            outs.append(solve(part, epsilon, max_iter, check=False, return_status=True))
+        else:
+            outs.append(solve_fn(part))
     assign = torch.cat([o[0].to(cost.device) for o in outs], dim=0)
     prices = torch.cat([o[1].to(cost.device) for o in outs], dim=0)
+    from . import _lib
+    for o in outs:
+        if len(o) > 2 and isinstance(o[-1], torch.Tensor) and o[-1].dtype == torch.int32:
+            _lib.check(int(o[-1].item()), f"auction kernel on {o[-1].device}")
     return assign, prices

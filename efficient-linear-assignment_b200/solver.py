@@ -31,9 +31,12 @@ def _as_schedule(epsilon: EpsArg) -> list[float]:
     return sched
 
 
-def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int) -> Tuple[
+def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int, tie_rule: int = 0) -> Tuple[
         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,)).
+
+    tie_rule: ``_lib.TIE_HIGHEST_ROW`` (0, the reference's election) or
+    ``_lib.TIE_LOWEST_ROW`` (1).
 
     The eager implementation: outputs allocated on the cost's device, one call
     of ``ela_auction_solve`` on the current stream (which also zeroes the status
@@ -55,7 +58,7 @@ def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int
     pdt = torch.float64 if code == 3 else torch.float32
     if dev.index is not None and dev.index != torch.cuda.current_device():
         with torch.cuda.device(dev):
-            return auction_solve(cost, eps, max_iter, path)
+            return auction_solve(cost, eps, max_iter, path, tie_rule)
     assign = torch.empty((B, N), dtype=torch.int64, device=dev)
     prices = torch.empty((B, M), dtype=pdt, device=dev)
     stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
@@ -74,21 +77,21 @@ def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int
     stream = torch.cuda.current_stream(dev).cuda_stream
     rc = lib.ela_auction_solve(
         cost.data_ptr(), code, B, N, M, cost.stride(0), cost.stride(1),
-        e, len(eps), int(max_iter), int(path), assign.data_ptr(),
+        e, len(eps), int(max_iter), int(path), int(tie_rule), assign.data_ptr(),
         prices.data_ptr(), stats.data_ptr(), status.data_ptr(), ws.data_ptr(), ws_bytes, stream)
     _lib.check(rc, "ela_auction_solve")
     return assign, prices, stats, status
 
 
 @torch.library.custom_op("ela::auction_solve", mutates_args=())
-def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int) -> Tuple[
+def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int, tie_rule: int = 0) -> Tuple[
         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,))."""
-    return auction_solve(cost, eps, max_iter, path)
+    return auction_solve(cost, eps, max_iter, path, tie_rule)
 
 
 @auction_solve_op.register_fake
-def _(cost, eps, max_iter, path):
+def _(cost, eps, max_iter, path, tie_rule=0):
     B, N, M = cost.shape
     pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
     return (cost.new_empty((B, N), dtype=torch.int64), cost.new_empty((B, M), dtype=pdt),
@@ -96,13 +99,16 @@ def _(cost, eps, max_iter, path):
 
 
 def solve(cost: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path: int = _lib.PATH_AUTO,
-          check: bool = True):
+          check: bool = True, return_status: bool = False, tie_rule: int = _lib.TIE_HIGHEST_ROW):
     """Solve a (B,N,M) or (N,M) CUDA cost tensor.
 
     epsilon: the reference's constant epsilon, or a schedule (one full solve per
     value, each starting from the previous prices).
-    Returns (assignment, prices, stats); with ``check`` the device status is read
-    back (one synchronisation) and a device-side error raises AuctionError.
+    tie_rule: which row wins among the bids on a column within 1e-5 of its new
+    price, ``TIE_HIGHEST_ROW`` (the reference) or ``TIE_LOWEST_ROW``.
+    Returns (assignment, prices, stats), plus the int32 device status word when
+    ``return_status``; with ``check`` the device status is read back (one
+    synchronisation) and a device-side error raises AuctionError.
     """
     squeeze = cost.dim() == 2
     if squeeze:
@@ -115,13 +121,15 @@ def solve(cost: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path
     # the custom op while torch.compile traces; the plain call (no dispatcher
     # overhead) in eager mode
     fn = auction_solve_op if torch.compiler.is_compiling() else auction_solve
-    assign, prices, stats, status = fn(cost.detach(), sched, int(max_iter), int(path))
+    if tie_rule not in (_lib.TIE_HIGHEST_ROW, _lib.TIE_LOWEST_ROW):
+        raise ValueError(f"unknown tie_rule {tie_rule}")
+    assign, prices, stats, status = fn(cost.detach(), sched, int(max_iter), int(path), int(tie_rule))
     if check:
         st = int(status.item())
         _lib.check(st, "auction kernel")
     if squeeze:
-        return assign[0], prices[0], stats[0]
-    return assign, prices, stats
+        assign, prices, stats = assign[0], prices[0], stats[0]
+    return (assign, prices, stats, status) if return_status else (assign, prices, stats)
 
 
 class AuctionB200:
@@ -133,13 +141,15 @@ class AuctionB200:
     contract as AuctionTorch (torch_backend.py:4-9,158).
     """
 
-    def __init__(self, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path: int = _lib.PATH_AUTO):
+    def __init__(self, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path: int = _lib.PATH_AUTO,
+                 tie_rule: int = _lib.TIE_HIGHEST_ROW):
         self.epsilon = epsilon
         self.max_iter = max_iter
         self.path = path
+        self.tie_rule = tie_rule
         self.last_stats = None
 
     def solve(self, cost_matrix: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
-        assign, prices, stats = solve(cost_matrix, self.epsilon, self.max_iter, self.path)
+        assign, prices, stats = solve(cost_matrix, self.epsilon, self.max_iter, self.path, tie_rule=self.tie_rule)
         self.last_stats = stats
         return assign, prices

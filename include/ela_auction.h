@@ -48,6 +48,15 @@ enum { ELA_DTYPE_F32 = 0, ELA_DTYPE_F16 = 1, ELA_DTYPE_BF16 = 2, ELA_DTYPE_F64 =
  *            distributed shared memory (few large problems; needs M >= 128) */
 enum { ELA_PATH_AUTO = 0, ELA_PATH_CTA = 1, ELA_PATH_GRID = 2, ELA_PATH_CLUSTER = 3 };
 
+/* Row tie rule of the election.  Among the bids on one column that lie within
+ * 1e-5 of its new price, ELA_TIE_HIGHEST_ROW (the reference's rule: torch's
+ * index_put_ with ascending rows keeps the last writer,
+ * src/efficient_linear_assignment/auction/torch_backend.py:126-136) elects the
+ * highest row; ELA_TIE_LOWEST_ROW elects the lowest.  Only HIGHEST_ROW gives
+ * the reference's indices; LOWEST_ROW is an equally valid auction (same bids,
+ * same prices, same epsilon-optimality bound). */
+enum { ELA_TIE_HIGHEST_ROW = 0, ELA_TIE_LOWEST_ROW = 1 };
+
 /* Library ABI version (major*100 + minor). */
 int ela_auction_version(void);
 
@@ -73,6 +82,8 @@ size_t ela_auction_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t M, i
  *               reference's constant-epsilon solve; n_eps > 1 runs one full
  *               solve per epsilon, each starting from the previous prices
  *   max_iter    bidding rounds allowed per epsilon (reference default 1000)
+ *   path        ELA_PATH_* (launch shape; every path gives the same results)
+ *   tie_rule    ELA_TIE_* (ELA_TIE_HIGHEST_ROW reproduces the reference)
  *   assign_out  device int64[B*N]; column of each row, -1 if unassigned
  *   prices_out  device float[B*M] (double[B*M] for ELA_DTYPE_F64)
  *   stats_out   device int64[B*4] or NULL: per problem
@@ -86,7 +97,7 @@ size_t ela_auction_workspace_bytes(int dtype, int64_t B, int64_t N, int64_t M, i
  */
 int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
                       int64_t stride_b, int64_t stride_n, const double* eps_schedule,
-                      int n_eps, int max_iter, int path, int64_t* assign_out,
+                      int n_eps, int max_iter, int path, int tie_rule, int64_t* assign_out,
                       void* prices_out, int64_t* stats_out, int32_t* status_out,
                       void* workspace, size_t workspace_bytes, void* stream);
 
@@ -128,8 +139,9 @@ void ela_auction_debug_skip_arrive(int on);
  * ELA_ERR_UNSUPPORTED before any work is enqueued.  The call allocates
  * nothing (no cudaMalloc, no cudaFree, no allocating library routine).
  *
- * The first call on a device looks up that device's address of the array
- * (cudaGetSymbolAddress, with the device current); make that first call
+ * The first call on a device (and the first after the device's context is
+ * replaced, e.g. by cudaDeviceReset) looks up that context's address of the
+ * array (cudaGetSymbolAddress, with the device current); make that first call
  * before any stream capture.  All calls on a device share the one array and
  * each call clears the part it uses, so calls whose work overlaps on the GPU
  * (different streams, or concurrent host threads) race and give wrong
@@ -137,9 +149,9 @@ void ela_auction_debug_skip_arrive(int on);
  */
 int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
                               int64_t stride_b, int64_t stride_n, const double* eps_schedule,
-                              int n_eps, int max_iter, int path, int64_t* assign_out,
-                              void* prices_out, int64_t* stats_out, int32_t* status_out,
-                              void* stream);
+                              int n_eps, int max_iter, int path, int tie_rule,
+                              int64_t* assign_out, void* prices_out, int64_t* stats_out,
+                              int32_t* status_out, void* stream);
 
 #ifdef __cplusplus
 }

@@ -212,7 +212,7 @@ DEFINE_TOPK(double, topk_row_d)
 #define DEFINE_SOLVER(R, NAME, LOADER, TOPK)                                                      \
     static void NAME(const void* cost, int dtype, int64_t off0, int64_t stride_n,           \
                      int64_t N, int64_t M, const double* eps, int n_eps, int max_iter,      \
-                     int64_t* assign, R* P, int64_t* stats, int inner_threads) {            \
+                     int tie_rule, int64_t* assign, R* P, int64_t* stats, int inner_threads) { \
         int64_t* owner = (int64_t*)malloc(sizeof(int64_t) * (size_t)(M > 0 ? M : 1));       \
         int64_t* active = (int64_t*)malloc(sizeof(int64_t) * (size_t)(N > 0 ? N : 1));      \
         int64_t* bidcol = (int64_t*)malloc(sizeof(int64_t) * (size_t)(N > 0 ? N : 1));      \
@@ -249,11 +249,12 @@ DEFINE_TOPK(double, topk_row_d)
                 for (k = 0; k < K; ++k) ties += tied[k];                                    \
                 /* scatter_reduce amax, include_self */                                     \
                 for (k = 0; k < K; ++k) { j = bidcol[k]; if (bid[k] > P[j]) P[j] = bid[k]; } \
-                /* election: ascending rows, last writer wins */                            \
+                /* election: ascending rows, last writer wins (tie_rule 0, the           \
+                   reference); tie_rule 1 keeps the first, i.e. the lowest row */           \
                 for (k = 0; k < K; ++k) {                                                   \
                     j = bidcol[k];                                                          \
                     R d = bid[k] - P[j]; if (d < 0) d = -d;                                 \
-                    if (d < win_tol) winner[j] = active[k];                                 \
+                    if (d < win_tol && (tie_rule == 0 || winner[j] < 0)) winner[j] = active[k]; \
                 }                                                                           \
                 /* ownership transfer; every won column appears once */                     \
                 for (k = 0; k < K; ++k) {                                                   \
@@ -284,10 +285,11 @@ DEFINE_SOLVER(double, solve_one_d, load_row_d, topk_row_d)
  */
 int ela_oracle_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
                      int64_t stride_b, int64_t stride_n, const double* eps, int n_eps,
-                     int max_iter, int64_t* assign_out, void* prices_out, int64_t* stats_out,
-                     int nthreads) {
+                     int max_iter, int tie_rule, int64_t* assign_out, void* prices_out,
+                     int64_t* stats_out, int nthreads) {
     if (B < 0 || N < 0 || M < 0 || n_eps < 1 || max_iter < 0) return 1;
     if (dtype < 0 || dtype > 3) return 1;
+    if (tie_rule != 0 && tie_rule != 1) return 1;
     if (N > 0 && M < 2) return 1; /* torch.topk(k=2) needs two columns */
     if (nthreads < 1) nthreads = 1;
     int outer = (B >= nthreads) ? nthreads : 1;
@@ -297,10 +299,10 @@ int ela_oracle_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t 
     for (b = 0; b < B; ++b) {
         if (dtype == ELA_F64)
             solve_one_d(cost, dtype, b * stride_b, stride_n, N, M, eps, n_eps, max_iter,
-                        assign_out + b * N, (double*)prices_out + b * M, stats_out + 4 * b, inner);
+                        tie_rule, assign_out + b * N, (double*)prices_out + b * M, stats_out + 4 * b, inner);
         else
             solve_one_f(cost, dtype, b * stride_b, stride_n, N, M, eps, n_eps, max_iter,
-                        assign_out + b * N, (float*)prices_out + b * M, stats_out + 4 * b, inner);
+                        tie_rule, assign_out + b * N, (float*)prices_out + b * M, stats_out + 4 * b, inner);
     }
     return 0;
 }

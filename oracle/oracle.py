@@ -43,7 +43,7 @@ def _load():
         lib.ela_oracle_solve.argtypes = [
             ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
             ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(ctypes.c_double), ctypes.c_int,
-            ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+            ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
         ]
         _lib = lib
     return _lib
@@ -59,10 +59,12 @@ def eps_schedule(eps0: float, eps_final: float, factor: float) -> list[float]:
     return out
 
 
-def solve(cost: torch.Tensor, eps, max_iter: int = 1000, nthreads: int = 1):
+def solve(cost: torch.Tensor, eps, max_iter: int = 1000, nthreads: int = 1, tie_rule: int = 0):
     """Oracle solve of a (B,N,M) CPU cost tensor.
 
     eps: a float (the reference's constant epsilon) or a list (epsilon schedule).
+    tie_rule: 0 = the reference's election (highest row among the bids within
+    1e-5 of the new price), 1 = lowest row (a variant, not the reference).
     Returns (assignment int64 (B,N) with -1 = unassigned, prices (B,M) float32 or
     float64, stats int64 (B,4) = [rounds, row_bids, tied_row_bids, unassigned]).
     """
@@ -79,7 +81,7 @@ def solve(cost: torch.Tensor, eps, max_iter: int = 1000, nthreads: int = 1):
     stats = torch.zeros((B, 4), dtype=torch.int64)
     rc = lib.ela_oracle_solve(
         ctypes.c_void_p(cost.data_ptr()), DTYPE_CODE[cost.dtype], B, N, M, N * M, M,
-        e_arr, len(sched), int(max_iter), ctypes.c_void_p(assign.data_ptr()),
+        e_arr, len(sched), int(max_iter), int(tie_rule), ctypes.c_void_p(assign.data_ptr()),
         ctypes.c_void_p(prices.data_ptr()), ctypes.c_void_p(stats.data_ptr()), int(nthreads))
     if rc != 0:
         raise ValueError(f"oracle rejected arguments (status {rc})")

@@ -32,7 +32,7 @@ def test_library_exports_every_declared_symbol():
 
 
 def test_status_strings_and_version():
-    assert _lib.load().ela_auction_version() >= 100
+    assert _lib.load().ela_auction_version() >= 200
     assert _lib.status_string(0) == "ok"
     assert "timed out" in _lib.status_string(3)
 
@@ -42,9 +42,14 @@ def test_solve_rejects_bad_arguments_without_touching_the_gpu():
     eps = (ctypes.c_double * 1)(1e-2)
     null = ctypes.c_void_p(0)
     # bad dtype
-    assert lib.ela_auction_solve(null, 9, 1, 8, 8, 64, 8, eps, 1, 10, 0, null, null, null, null, null, 0, null) == 1
+    assert lib.ela_auction_solve(null, 9, 1, 8, 8, 64, 8, eps, 1, 10, 0, 0, null, null, null, null, null, 0, null) == 1
     # epsilon must be > 0
     bad = (ctypes.c_double * 1)(0.0)
-    assert lib.ela_auction_solve(null, 0, 1, 8, 8, 64, 8, bad, 1, 10, 0, null, null, null, null, null, 0, null) == 1
+    assert lib.ela_auction_solve(null, 0, 1, 8, 8, 64, 8, bad, 1, 10, 0, 0, null, null, null, null, null, 0, null) == 1
+    # unknown tie rule (checked before any device work)
+    one = ctypes.c_void_p(256)
+    assert lib.ela_auction_solve(one, 0, 1, 8, 8, 64, 8, eps, 1, 10, 0, 7, one, one, null, null, one, 1 << 20,
+                                 null) == 1
+    assert lib.ela_auction_solve_noalloc(one, 0, 1, 8, 8, 64, 8, eps, 1, 10, 0, 7, one, one, null, null, null) == 1
     # empty batch is a no-op
-    assert lib.ela_auction_solve(null, 0, 0, 8, 8, 64, 8, eps, 1, 10, 0, null, null, null, null, null, 0, null) == 0
+    assert lib.ela_auction_solve(null, 0, 0, 8, 8, 64, 8, eps, 1, 10, 0, 0, null, null, null, null, null, 0, null) == 0

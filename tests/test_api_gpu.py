@@ -131,8 +131,10 @@ def test_multi_device_sharding_matches_single_solve():
     cost = ela.workloads.cfg4(B=12, N=128).to(dev)
     ref_a, ref_p, _ = ela.solve(cost, 1e-2)
     devs = [torch.device("cuda", i) for i in range(torch.cuda.device_count())]
-    a, p = solve_multi_device(cost, devs, lambda c: ela.solve(c, 1e-2)[:2])
+    a, p = solve_multi_device(cost, devs, epsilon=1e-2)  # default: no synchronisation between devices
     assert torch.equal(a, ref_a) and torch.equal(p, ref_p)
+    a2, p2 = solve_multi_device(cost, devs, lambda c: ela.solve(c, 1e-2, return_status=True, check=False))
+    assert torch.equal(a2, ref_a) and torch.equal(p2, ref_p)
 
 
 @pytest.mark.parametrize("shape", [(2, 13, 21), (1, 16, 21), (1, 13, 16), (3, 7, 9)])
