@@ -377,6 +377,7 @@ struct Params {
     int max_wpr;             // most warps that share one row's scan (power of two)
     int team;                // cluster path: clusters per problem
     int tie_rule;            // ELA_TIE_*: which row wins among bids within 1e-5 of the new price
+    int cache_k;             // one-CTA path: row-cache entries per row (0: no cache)
     size_t team_bytes;       // cluster path: workspace bytes per team
 };
 
@@ -698,6 +699,150 @@ __device__ __forceinline__ void finish_bid(const Params& p, const In* row, const
     bid_out = add_rn(Ps[j1], add_rn(sub_rn(t.v1, t.v2), eps));
 }
 
+// ------------------------------------------------------------- row cache
+// Prices never fall during a solve (a new price is the column's maximum bid,
+// never below the old price, and each epsilon phase starts from the previous
+// phase's prices), and fl((-c) - P) is non-increasing in P, so every value
+// v[j] of a row only falls.  After a full scan of row i the cache keeps the
+// entries S = {(j, c[i][j]) : v[j] > tau}; tau bounds every column outside S
+// then, and so at every later time.  A later bid of the row recomputes the
+// values of S with the current prices: if their second value is still above
+// tau, the row's exact top-2 lies in S, including every occurrence of a tied
+// maximum (all of them are above tau), so the bid equals a full scan's.
+// Otherwise the row is scanned again and S rebuilt.  One warp per row; at
+// most 32 entries, one per lane.
+
+// Top-2 of row i from its cache (exact, ties included); true if it is the
+// row's top-2 (second value above the cache's bound).
+template <typename R>
+__device__ __forceinline__ bool cache_top2(const R* __restrict__ Ps, const unsigned short* ccol, const R* ccost,
+                                           int n, R tau, int lane, Top2<R>& t) {
+    top2_init(t);
+    if (lane < n) {
+        const int j = ccol[lane];
+        t.v1 = sub_rn(-ccost[lane], Ps[j]);
+        t.p1 = j;
+    }
+    t = top2_warp(t);
+    return t.v2 > tau;
+}
+
+// Full scan of a row of M = NCH*32*W columns held in registers (lane l has the
+// 16-byte chunks l, l+32, ...), exact top-2 with ties, then a new cache: the
+// threshold search looks for the lowest tau with at most kc values above it
+// (interpolating the count between a bound that holds too many and one that
+// holds few enough; every lane's maximum exceeds the lowest lane maximum, so
+// that bound starts the search), then the values above tau are compacted into
+// the cache with ballots.
+template <typename In, int NCH>
+__device__ __noinline__ Top2<float> scan_build(const In* row, const float* __restrict__ Ps, int lane, int kc,
+                                               unsigned short* ccol, float* ccost, float* ctau, unsigned char* ccnt) {
+    constexpr int W = Elem<In>::W, NV = NCH * W;
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    uint4 raw[NCH];
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) raw[u] = ld_stream16(rv + lane + 32 * u);
+    float v[NV];
+    Top2<float> t;
+    top2_init(t);
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+        float x[W], pr[W];
+        Elem<In>::template unpack<float>(raw[u], x);
+        load_prices<float, W>(Ps, (lane + 32 * u) * W, pr);
+#pragma unroll
+        for (int e = 0; e < W; ++e) {
+            v[u * W + e] = sub_rn(-x[e], pr[e]);
+            top2_add(t, v[u * W + e], (lane + 32 * u) * W + e);
+        }
+    }
+    const unsigned int lane_max_key = fkey(t.v1);
+    const Top2<float> r = top2_warp(t);
+    auto count_above = [&](float th) {
+        int c = 0;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) c += (v[k] > th) ? 1 : 0;
+        return (int)__reduce_add_sync(0xffffffffu, (unsigned int)c);
+    };
+    float hi = r.v1, lo = fkey_inv(__reduce_min_sync(0xffffffffu, lane_max_key));
+    int hic = 0, loc = count_above(lo);
+    if (loc <= kc) {
+        hi = lo;
+        hic = loc;
+    } else {
+        const float target = 0.95f * (float)kc;
+        for (int it = 0; it < 6; ++it) {
+            float th = hi - (hi - lo) * ((target - (float)hic) / (float)(loc - hic));
+            if (!(th > lo && th < hi)) th = 0.5f * (lo + hi);
+            const int m = count_above(th);
+            if (m <= kc) {
+                hi = th;
+                hic = m;
+                if (m >= kc - kc / 8) break;
+            } else {
+                lo = th;
+                loc = m;
+            }
+        }
+    }
+    int base = 0;
+#pragma unroll
+    for (int u = 0; u < NCH; ++u) {
+        float x[W];
+        Elem<In>::template unpack<float>(raw[u], x);
+#pragma unroll
+        for (int e = 0; e < W; ++e) {
+            const bool keep = v[u * W + e] > hi;
+            const unsigned int m = __ballot_sync(0xffffffffu, keep);
+            if (keep) {
+                const int pos = base + __popc(m & ((1u << lane) - 1u));
+                ccol[pos] = (unsigned short)((lane + 32 * u) * W + e);
+                ccost[pos] = x[e];
+            }
+            base += __popc(m);
+        }
+    }
+    if (lane == 0) { *ctau = hi; *ccnt = (unsigned char)hic; }
+    return r;
+}
+
+// One cached row's bid (one warp): from the cache when it still holds the
+// row's top-2, else from a full scan that rebuilds the cache.  Rows of
+// nch * 32 16-byte chunks, nch <= 32 / W (at most 32 values per lane).
+// Returns the column bid on; *bid_out gets the bid.
+template <typename In>
+__device__ __noinline__ int cached_row_bid(int nch, const In* row, const float* __restrict__ Ps, float eps, int lane,
+                                           int kc, unsigned short* ccol, float* ccost, float* ctau,
+                                           unsigned char* ccnt, float* bid_out) {
+    constexpr int W = Elem<In>::W;
+    Top2<float> tt;
+    const int n = *ccnt;
+    bool hit = false;
+    if (n >= 2) hit = cache_top2<float>(Ps, ccol, ccost, n, *ctau, lane, tt);
+    if (!hit) {
+        switch (nch) {
+        case 1: tt = scan_build<In, 1>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+        case 2: tt = scan_build<In, 2>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+        case 3: tt = scan_build<In, 3>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+        default:
+            if constexpr (W == 4) {
+                switch (nch) {
+                case 4: tt = scan_build<In, 4>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+                case 5: tt = scan_build<In, 5>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+                case 6: tt = scan_build<In, 6>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+                case 7: tt = scan_build<In, 7>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+                default: tt = scan_build<In, 8>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+                }
+            } else {
+                tt = scan_build<In, 4>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt);
+            }
+        }
+    }
+    const int j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
+    *bid_out = add_rn(Ps[j1], add_rn(sub_rn(tt.v1, tt.v2), eps));
+    return j1;
+}
+
 // ------------------------------------------------------ bid exchange (S > 1)
 // Each CTA of a group publishes its round-t bids in its own segment of the
 // round's buffer (two buffers, by round parity):
@@ -855,12 +1000,14 @@ __device__ bool read_extra_entries(const unsigned char* segbase, size_t seg_byte
 // ================================================================== kernel
 // Shared-memory layout (byte offsets), identical on host and device.
 struct KLayout {
-    size_t P, maxb, win, owner, lbid, lrow, lcol, rowcol, rowbid, active, wtop, scr_v, scr_i, total;
+    size_t P, maxb, win, owner, lbid, lrow, lcol, rowcol, rowbid, active, wtop, scr_v, scr_i;
+    size_t ccol, ccost, ctau, ccnt;  // row cache (kc > 0)
+    size_t total;
 };
 __host__ __device__ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 template <typename R>
-__host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int warps) {
+__host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int warps, int kc = 0) {
     KLayout L;
     size_t o = 0;
     L.P = o;      o = align_up(o + sizeof(R) * (size_t)M, 16);   // prices
@@ -877,6 +1024,10 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
     const size_t scr = (M < ELA_SMALL_M) ? (size_t)warps * ELA_SMALL_M : 0;
     L.scr_v = o;  o = align_up(o + sizeof(R) * scr, 16);
     L.scr_i = o;  o = align_up(o + 4 * scr, 16);
+    L.ccost = o;  o = align_up(o + sizeof(R) * (size_t)rpc * kc, 16);  // row cache: cost of each entry
+    L.ccol = o;   o = align_up(o + 2 * (size_t)rpc * kc, 16);          //             column of each entry
+    L.ctau = o;   o = align_up(o + sizeof(R) * (size_t)(kc ? rpc : 0), 16);  // bound on every other column
+    L.ccnt = o;   o = align_up(o + (size_t)(kc ? rpc : 0), 16);        //             entries (0: none)
     L.total = o;
     return L;
 }
@@ -899,12 +1050,13 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 //                   a round's bids go straight into the CTA's shared list.
 //   MULTI == true:  S CTAs share a problem; CTA c owns the block of rows
 //                   [c*rpc, (c+1)*rpc), rpc = ceil(N/S) (few TLB pages per CTA)
-template <typename In, typename R, bool MULTI, int THREADS, int MINB>
+template <typename In, typename R, bool MULTI, int THREADS, int MINB, bool CACHE = false>
 __global__ void __launch_bounds__(THREADS, MINB)
 auction_kernel(const Params p) {
+    static_assert(!CACHE || (!MULTI && std::is_same<R, float>::value), "row cache: one-CTA path, fp32 prices");
     typedef Bits<R> BT;
     typedef typename BT::U U;
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_nact, s_total, s_extra, s_fail;
     __shared__ int s_ties, s_exact;  // rows whose maximum tied; scan exactly first when many do
     __shared__ int s_cnt[MULTI ? ELA_MAX_S : 1], s_off[MULTI ? ELA_MAX_S : 1];
@@ -917,7 +1069,8 @@ auction_kernel(const Params p) {
     const int N = (int)p.N, M = (int)p.M;
     const int row0 = c * p.rows_per_cta;                           // first owned row
     const int my_rows = (row0 < N) ? min(p.rows_per_cta, N - row0) : 0;
-    const KLayout L = k_layout<R>(N, M, p.rows_per_cta, nw);
+    const int kc = CACHE ? p.cache_k : 0;
+    const KLayout L = k_layout<R>(N, M, p.rows_per_cta, nw, kc);
     R* P = reinterpret_cast<R*>(smem + L.P);
     U* maxb = reinterpret_cast<U*>(smem + L.maxb);
     int* win = reinterpret_cast<int*>(smem + L.win);
@@ -945,6 +1098,8 @@ auction_kernel(const Params p) {
         const In* base = reinterpret_cast<const In*>(p.cost) + b * p.stride_b;
         for (int j = tid; j < M; j += blockDim.x) { P[j] = (R)0; maxb[j] = 0; win[j] = 0; owner[j] = -1; }
         for (int q = tid; q < my_rows; q += blockDim.x) { rowcol[q] = -1; rowbid[q] = -1; }
+        if (kc)
+            for (int q = tid; q < my_rows; q += blockDim.x) smem[L.ccnt + q] = 0;  // row caches empty
         long long rounds = 0, rowbids = 0;
         int ph = 0, it = 0;
         R eps = (R)p.eps[0];  // this epsilon (read once per epsilon)
@@ -1009,6 +1164,22 @@ auction_kernel(const Params p) {
                         else put_entry<R>(myseg, k, t1, row0 + q, j1, bid);
                     }
                 };
+                if constexpr (CACHE) {
+                        // cached rows: a bid from the row's cache, else a full scan
+                        // that rebuilds it (one warp per row)
+                        const KLayout LC = k_layout<R>(N, M, N, nw, kc);
+                        const int nch = M / (32 * Elem<In>::W);  // 16-byte chunks per lane of a cached row
+                        for (int k = warp; k < K; k += nw) {
+                            const int q = active[k];
+                            float bid;
+                            const int j1 = cached_row_bid<In>(
+                                nch, base + (int64_t)q * p.stride_n, P, eps, lane, kc,
+                                reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc,
+                                reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc,
+                                reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q, &bid);
+                            if (lane == 0) { rowbid[q] = j1; lbid[k] = bid; lrow[k] = q; lcol[k] = j1; }
+                        }
+                } else {
                 if (lw == 0 && K > nw && !s_exact && p.vec_ok) {
                     // several rows per warp: two at a time (no CTA barrier in here)
                     for (int kb = 0; kb < K; kb += 2 * nw) {
@@ -1084,6 +1255,7 @@ auction_kernel(const Params p) {
                     }
                     if (wpr > 1 && kb + groups < K) __syncthreads();  // wtop is reused
                 }
+                }  // !CACHE
             }
             __syncthreads();
             if (tid == 0) { s_exact = (K > 0) ? (s_ties * 4 > K) : s_exact; s_ties = 0; }
@@ -1359,13 +1531,15 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int p
                                           const volatile int* abort) {
     const unsigned int a = smem_addr(mb);
     const unsigned long long t0 = globaltimer_ns();
-    for (;;) {
+    for (unsigned int spins = 1;; ++spins) {
         unsigned int done;
         asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
                      : "=r"(done) : "r"(a), "r"(parity) : "memory");
         if (done) return true;
-        if (*abort) return false;
-        if (globaltimer_ns() - t0 > limit_ns) return false;
+        if ((spins & 15u) == 0) {  // slow path: a peer's failure mark, the time limit
+            if (*abort) return false;
+            if (globaltimer_ns() - t0 > limit_ns) return false;
+        }
     }
 }
 
@@ -1401,6 +1575,22 @@ __device__ int compact_unassigned(const IX* rowcol, int N, IX* act, int* s_scan)
     return total;
 }
 
+// The cluster's failure exit (see the kernel): marks the abort flag, marks
+// every peer's s_abort unless this CTA learned of the failure from its own,
+// then arrives at and waits on the cluster barrier.  Kept out of line so that
+// the round loop's code does not change for a path it never takes.
+__device__ __noinline__ void cluster_leave(int* abort_flag, bool pending, int* s_abort, int CS) {
+    const int tid = threadIdx.x;
+    if (tid == 0) atomicExch(abort_flag, 1);
+    if (pending) cluster_wait_acquire();
+    if (tid < CS && !*(volatile int*)s_abort) {
+        const unsigned int ra = cluster_map(smem_addr(s_abort), tid);
+        asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(ra), "r"(1) : "memory");
+    }
+    cluster_arrive_release();
+    cluster_wait_acquire();
+}
+
 // Team layout: ngroups teams of p.team clusters; a team solves one problem at
 // a time.  Large rounds use every CTA of the team (rows split over the team;
 // bids exchanged through distributed shared memory when the team is one
@@ -1414,7 +1604,7 @@ auction_cluster_kernel(const Params p) {
     namespace cg = cooperative_groups;
     typedef Bits<R> BT;
     typedef typename BT::U U;
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(128) unsigned char smem[];
     __shared__ int s_scan[32];
     __shared__ int s_cnt, s_total, s_extra, s_fail;
     __shared__ int s_ties, s_exact;  // rows whose maximum tied; scan exactly first when many do
@@ -1487,15 +1677,9 @@ auction_cluster_kernel(const Params p) {
     // failing peer's mark is released before its arrival) and then leaves the
     // same way without storing to peers, since a failed peer may have exited.
     // Waits count only resident CTAs, so the last leavers do not block.
-    auto leave = [&]() {
-        if (tid == 0) atomicExch(abort_flag, 1);
-        if (cl_pending) { cluster_wait_acquire(); cl_pending = false; }
-        if (tid < CS && !*(volatile int*)&s_abort) *cluster.map_shared_rank(&s_abort, tid) = 1;
-        cluster_arrive_release();
-        cluster_wait_acquire();
-    };
+#define ELA_CLUSTER_LEAVE() do { cluster_leave(abort_flag, cl_pending, &s_abort, CS); return; } while (0)
     // (read once per CTA: every thread of the CTA must take the same way)
-#define ELA_CLUSTER_ABORT_CHECK() do { if (__syncthreads_or(*(volatile int*)&s_abort)) { leave(); return; } } while (0)
+#define ELA_CLUSTER_ABORT_CHECK() do { if (__syncthreads_or(*(volatile int*)&s_abort)) ELA_CLUSTER_LEAVE(); } while (0)
 
 #ifdef ELA_PROF
     if (blockIdx.x == 0 && threadIdx.x == 0) { g_trace[8191][0] = clock64(); g_trace[8191][1] = globaltimer_ns(); }
@@ -1551,7 +1735,7 @@ auction_cluster_kernel(const Params p) {
                             s_fail = !ok;
                         }
                         __syncthreads();
-                        if (s_fail) { leave(); return; }
+                        if (s_fail) ELA_CLUSTER_LEAVE();
                         for (int j = tid; j < M; j += blockDim.x) P[j] = __ldcg(pbuf + j);
                     }
                 }
@@ -1616,8 +1800,7 @@ auction_cluster_kernel(const Params p) {
                     __syncthreads();
                     if (s_fail) {
                         if (tid == 0 && !*(volatile int*)&s_abort) atomicCAS(p.status, ELA_OK, ELA_ERR_TIMEOUT);
-                        leave();
-                        return;
+                        ELA_CLUSTER_LEAVE();
                     }
                     ++sr;
                 } else {
@@ -1833,13 +2016,11 @@ auction_cluster_kernel(const Params p) {
                     }
                 }
                 __syncthreads();
-                if (s_fail) { leave(); return; }
+                if (s_fail) ELA_CLUSTER_LEAVE();
                 if (s_extra && !read_extra_entries<R, IX>(tb + (size_t)((t & 1) * ST) * p.seg_bytes, p.seg_bytes, ST,
                                                           s_segcnt, s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag,
-                                                          p.status)) {
-                    leave();
-                    return;
-                }
+                                                          p.status))
+                    ELA_CLUSTER_LEAVE();
                 nent = s_total;
                 compact = true;
                 ++t;
@@ -1936,6 +2117,7 @@ auction_cluster_kernel(const Params p) {
 #endif
     cluster.sync();  // no remote store may target a CTA that has exited
 #undef ELA_CLUSTER_ABORT_CHECK
+#undef ELA_CLUSTER_LEAVE
 }
 
 }  // namespace
@@ -1956,6 +2138,7 @@ struct Plan {
     size_t smem;       // dynamic shared memory per CTA
     size_t seg_bytes;  // S > 1
     size_t ws_bytes;   // total workspace
+    int cache_k;       // one-CTA path: row-cache entries per row
 };
 
 int elem_size(int dtype) {
@@ -2001,9 +2184,27 @@ int cluster_fit(int cs, size_t smem) {
     return n;
 }
 
+// Row-cache entries per row on the one-CTA path: the most (32, 28, ..., 16)
+// whose shared memory still lets ELA_MINB_ONE CTAs share an SM, for fp32
+// prices and rows of 128..1024 columns that are whole 16-byte chunks per lane;
+// 0 (no cache) otherwise.  ELA_ROW_CACHE=0 turns it off (tuning knob).
 template <typename R>
-int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_max, Plan& pl) {
-    const size_t one_smem = k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32).total;
+int row_cache_k(int64_t N, int64_t M, int es, size_t smem_cta) {
+    if (!std::is_same<R, float>::value || es == 0) return 0;
+    if (const char* env = getenv("ELA_ROW_CACHE"))
+        if (atoi(env) == 0) return 0;
+    const int64_t per_lane = 32 * (16 / es);  // columns per 16-byte chunk slot of a warp
+    if (M < ELA_SMALL_M || M % per_lane != 0 || M / per_lane > 8 || M > 65535) return 0;
+    for (int kc = 32; kc >= 16; kc -= 4)
+        if (k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32, kc).total <= smem_cta) return kc;
+    return 0;
+}
+
+template <typename R>
+int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_max, size_t smem_sm, int es,
+                Plan& pl) {
+    const int kc = row_cache_k<R>(N, M, es, smem_sm / ELA_MINB_ONE - 1024 - 3 * 1024);
+    const size_t one_smem = k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32, kc).total;
     const bool one_fits = one_smem <= smem_max;
     int ngroups = 1;
     const int S = ctas_per_problem(B, N, sms, ngroups);
@@ -2085,6 +2286,7 @@ int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_
         if (!one_fits) return ELA_ERR_UNSUPPORTED;
         pl.S = 1; pl.ngroups = 0; pl.rpc = (int)N;
         pl.smem = one_smem;
+        pl.cache_k = kc;
         pl.seg_bytes = 0;
         pl.ws_bytes = ELA_WS_HEADER;
     } else if (chosen == ELA_PATH_GRID) {
@@ -2099,7 +2301,7 @@ int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_
     return ELA_OK;
 }
 
-int device_limits(int& sms, size_t& smem_max) {
+int device_limits(int& sms, size_t& smem_max, size_t& smem_sm) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return ELA_ERR_CUDA;
     int v = 0;
@@ -2107,6 +2309,8 @@ int device_limits(int& sms, size_t& smem_max) {
     sms = v;
     if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess) return ELA_ERR_CUDA;
     smem_max = (size_t)v - 3 * 1024;  // room for the kernel's static shared variables
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess) return ELA_ERR_CUDA;
+    smem_sm = (size_t)v;
     return ELA_OK;
 }
 
@@ -2116,13 +2320,14 @@ int make_plan_uncached(int dtype, int64_t B, int64_t N, int64_t M, int path, Pla
     if (N > 0 && M < 2) return ELA_ERR_ARGUMENT;
     if (N >= (1ll << 30) || M >= (1ll << 30)) return ELA_ERR_UNSUPPORTED;
     int sms = 0;
-    size_t smem_max = 0;
-    const int rc = device_limits(sms, smem_max);
+    size_t smem_max = 0, smem_sm = 0;
+    const int rc = device_limits(sms, smem_max, smem_sm);
     if (rc != ELA_OK) return rc;
     if (!allow_cluster && path == ELA_PATH_CLUSTER) return ELA_ERR_UNSUPPORTED;
     const int ask = (!allow_cluster && path == ELA_PATH_AUTO) ? -1 : path;
-    return dtype == ELA_DTYPE_F64 ? make_plan_t<double>(B, N, M, ask, sms, smem_max, pl)
-                                  : make_plan_t<float>(B, N, M, ask, sms, smem_max, pl);
+    const int es = elem_size(dtype);
+    return dtype == ELA_DTYPE_F64 ? make_plan_t<double>(B, N, M, ask, sms, smem_max, smem_sm, es, pl)
+                                  : make_plan_t<float>(B, N, M, ask, sms, smem_max, smem_sm, es, pl);
 }
 
 // Plans are cached per device, sizes, path and tuning-knob settings: planning
@@ -2136,9 +2341,9 @@ int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bo
     if (cudaGetDevice(&dev) != cudaSuccess) return ELA_ERR_CUDA;
     char key[256];
     auto knob = [](const char* name) { const char* v = getenv(name); return v ? v : "-"; };
-    snprintf(key, sizeof key, "%d|%d|%lld|%lld|%lld|%d|%d|%.16s|%.16s|%.16s", dev, dtype, (long long)B, (long long)N,
-             (long long)M, path, allow_cluster ? 1 : 0, knob("ELA_CTAS_PER_PROBLEM"), knob("ELA_CLUSTER_SIZE"),
-             knob("ELA_CLUSTERS_PER_PROBLEM"));
+    snprintf(key, sizeof key, "%d|%d|%lld|%lld|%lld|%d|%d|%.16s|%.16s|%.16s|%.16s", dev, dtype, (long long)B,
+             (long long)N, (long long)M, path, allow_cluster ? 1 : 0, knob("ELA_CTAS_PER_PROBLEM"),
+             knob("ELA_CLUSTER_SIZE"), knob("ELA_CLUSTERS_PER_PROBLEM"), knob("ELA_ROW_CACHE"));
     {
         std::lock_guard<std::mutex> lock(g_plan_mu);
         auto it = g_plans.find(key);
@@ -2180,6 +2385,8 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
         // co-schedule, and a refused team plan falls back to one cluster per
         // problem (no inter-cluster waits; same results).
         cfg.numAttrs = pl.team > 1 ? 2 : 1;
+        if (const char* env = getenv("ELA_TEAM_COOPERATIVE"))  // tuning knob (A/B of the co-scheduling guarantee)
+            if (atoi(env) == 0) cfg.numAttrs = 1;
         cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
         if (e != cudaSuccess && pl.team > 1) {
             cudaGetLastError();  // the refused launch left no work behind
@@ -2199,6 +2406,8 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
     }
     if (pl.S == 1) {
         auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE>;
+        if constexpr (std::is_same<R, float>::value)
+            if (p.cache_k > 0) kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, true>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
         const int64_t grid = p.B < (1ll << 20) ? p.B : (1ll << 20);
@@ -2393,6 +2602,7 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
     p.rows_per_cta = pl.rpc;
     p.team = pl.team;
     p.team_bytes = pl.team_bytes;
+    p.cache_k = p.vec_ok ? pl.cache_k : 0;
     if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
@@ -2431,6 +2641,7 @@ int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N,
     p.rows_per_cta = pl.rpc;
     p.team = pl.team;
     p.team_bytes = pl.team_bytes;
+    p.cache_k = p.vec_ok ? pl.cache_k : 0;
     // The array keeps the previous call's contents: clear the part this solve
     // uses (abort flag, status word, exchange tags must start at zero).
     if (cudaMemsetAsync(scratch, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;

@@ -67,11 +67,11 @@ def test_lowest_row_rule_matches_oracle_and_bound(path, oracle_mod):
     cases = [
         (torch.rand(2, 256, 256, generator=g), 1e-3),
         ((torch.rand(3, 136, 136, generator=g) * 6).floor(), 1.0 / 137),  # integer costs: ties
-        (ela.workloads.cfg5(2, 512), [16.0, 1.0, 1.0 / 513]),
+        (ela.workloads.cfg5(2, 512), ela.workloads.eps_schedule(16.0, 1.0 / 513, 0.25)),  # convergent mode
     ]
     for cost, eps in cases:
-        a, p, st = ela.solve(cost.cuda(), eps, 5000, path=path, tie_rule=ela.TIE_LOWEST_ROW)
-        ao, po, so = oracle_mod.solve(cost, eps, 5000, nthreads=4, tie_rule=1)
+        a, p, st = ela.solve(cost.cuda(), eps, 20000, path=path, tie_rule=ela.TIE_LOWEST_ROW)
+        ao, po, so = oracle_mod.solve(cost, eps, 20000, nthreads=4, tie_rule=1)
         assert torch.equal(a.cpu(), ao) and torch.equal(p.cpu(), po)
         assert torch.equal(st[:, :2].cpu(), so[:, :2])
         eps_final = eps[-1] if isinstance(eps, list) else eps
