@@ -843,6 +843,19 @@ __device__ __noinline__ int cached_row_bid(int nch, const In* row, const float* 
     return j1;
 }
 
+// One row's bid by one warp from a full scan (exact top-2 on a tied
+// maximum); returns the column, *bid_out the bid.  Out of line: it serves the
+// one-bidder chains of the one-CTA kernel, whose registers stay free.
+template <typename In, typename R>
+__device__ __noinline__ int plain_row_bid(const Params& p, const In* row, const R* __restrict__ Ps, R eps, int lane,
+                                          R* scr_v, int* scr_i, R* bid_out) {
+    Top2<R> tt = scan_row_fast<In, R>(p, row, Ps, lane, 0, 1);
+    if (p.M >= ELA_SMALL_M && tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, Ps, lane, 0, 1);
+    int j1;
+    finish_bid<In, R>(p, row, Ps, tt, eps, lane, scr_v, scr_i, j1, *bid_out);
+    return j1;
+}
+
 // ------------------------------------------------------ bid exchange (S > 1)
 // Each CTA of a group publishes its round-t bids in its own segment of the
 // round's buffer (two buffers, by round parity):
@@ -1062,6 +1075,7 @@ auction_kernel(const Params p) {
     __shared__ int s_cnt[MULTI ? ELA_MAX_S : 1], s_off[MULTI ? ELA_MAX_S : 1];
     __shared__ int s_exoff[MULTI ? ELA_MAX_S + 1 : 1];
     __shared__ int s_unassigned;
+    __shared__ int s_chain;  // one-bidder rounds run by warp 0 alone
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
     const int S = MULTI ? p.S : 1;
@@ -1130,6 +1144,61 @@ auction_kernel(const Params p) {
             if (tid == 0) { s_total = 0; s_extra = 0; s_fail = 0; }
             __syncthreads();
             const int K = s_nact;
+            if constexpr (!MULTI) {
+                if (K == 1) {
+                    // ---- a chain of rounds with one bidder each, run by warp 0
+                    //      alone (no CTA barrier, no election arrays): the only
+                    //      bid sets the column's price (a bid never falls below
+                    //      the old price) and wins it, and the evicted owner, if
+                    //      any, is the next round's only bidder.  Identical to
+                    //      running those rounds one by one.
+                    if (warp == 0) {
+                        int q = active[0], n = 0;
+                        for (;;) {
+                            const In* row = base + (int64_t)q * p.stride_n;
+                            int j1;
+                            R bid;
+                            if constexpr (CACHE) {
+                                const KLayout LC = k_layout<R>(N, M, N, nw, kc);
+                                float fb;
+                                j1 = cached_row_bid<In>(M / (32 * Elem<In>::W), row, P, eps, lane, kc,
+                                                        reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc,
+                                                        reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc,
+                                                        reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q,
+                                                        &fb);
+                                bid = fb;
+                            } else {
+                                j1 = plain_row_bid<In, R>(p, row, P, eps, lane, scr_v, scr_i, &bid);
+                            }
+                            const int prev = owner[j1];
+                            __syncwarp();  // every lane has read P and owner before they change
+                            if (lane == 0) {
+                                P[j1] = bid;
+                                owner[j1] = q;
+                                rowcol[q] = j1;
+                                if (prev >= 0) rowcol[prev] = -1;
+                            }
+                            __syncwarp();
+                            ++n;
+                            if (prev < 0 || it + n == p.max_iter) {
+                                if (lane == 0) {
+                                    s_nact = prev >= 0 ? 1 : 0;
+                                    if (prev >= 0) active[0] = prev;
+                                    s_chain = n;
+                                }
+                                break;
+                            }
+                            q = prev;
+                        }
+                    }
+                    __syncthreads();
+                    const int n = s_chain;
+                    rounds += n;
+                    rowbids += n;
+                    it += n;
+                    continue;
+                }
+            }
             PROF_MARK(pt1);
             unsigned long long* myseg =
                 reinterpret_cast<unsigned long long*>(gbase + (size_t)((t & 1) * S + c) * p.seg_bytes);
@@ -2139,6 +2208,7 @@ struct Plan {
     size_t seg_bytes;  // S > 1
     size_t ws_bytes;   // total workspace
     int cache_k;       // one-CTA path: row-cache entries per row
+    int one_threads;   // one-CTA path: threads per CTA (256: two CTAs per SM; 512: one)
 };
 
 int elem_size(int dtype) {
@@ -2189,22 +2259,31 @@ int cluster_fit(int cs, size_t smem) {
 // prices and rows of 128..1024 columns that are whole 16-byte chunks per lane;
 // 0 (no cache) otherwise.  ELA_ROW_CACHE=0 turns it off (tuning knob).
 template <typename R>
-int row_cache_k(int64_t N, int64_t M, int es, size_t smem_cta) {
+int row_cache_k(int64_t N, int64_t M, int es, size_t smem_cta, int warps) {
     if (!std::is_same<R, float>::value || es == 0) return 0;
     if (const char* env = getenv("ELA_ROW_CACHE"))
         if (atoi(env) == 0) return 0;
     const int64_t per_lane = 32 * (16 / es);  // columns per 16-byte chunk slot of a warp
     if (M < ELA_SMALL_M || M % per_lane != 0 || M / per_lane > 8 || M > 65535) return 0;
     for (int kc = 32; kc >= 16; kc -= 4)
-        if (k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32, kc).total <= smem_cta) return kc;
+        if (k_layout<R>(N, M, (int)N, warps, kc).total <= smem_cta) return kc;
     return 0;
 }
 
 template <typename R>
 int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_max, size_t smem_sm, int es,
                 Plan& pl) {
-    const int kc = row_cache_k<R>(N, M, es, smem_sm / ELA_MINB_ONE - 1024 - 3 * 1024);
-    const size_t one_smem = k_layout<R>(N, M, (int)N, ELA_THREADS_ONE / 32, kc).total;
+    // one CTA per problem: 256 threads, two CTAs per SM, while the batch
+    // outnumbers the SMs; otherwise (B <= SMs: a batch sharded over several
+    // GPUs) one CTA of 512 threads per SM, twice the warps for the wide early
+    // rounds and the whole SM's shared memory for the row cache
+    bool wide = B <= sms;
+    if (const char* env = getenv("ELA_WIDE_CTA"))  // tuning knob
+        if (atoi(env) == 0) wide = false;
+    const int one_threads = wide ? ELA_THREADS_MULTI : ELA_THREADS_ONE;
+    const int kc = row_cache_k<R>(N, M, es, wide ? smem_max : smem_sm / ELA_MINB_ONE - 1024 - 3 * 1024,
+                                  one_threads / 32);
+    const size_t one_smem = k_layout<R>(N, M, (int)N, one_threads / 32, kc).total;
     const bool one_fits = one_smem <= smem_max;
     int ngroups = 1;
     const int S = ctas_per_problem(B, N, sms, ngroups);
@@ -2287,6 +2366,7 @@ int make_plan_t(int64_t B, int64_t N, int64_t M, int path, int sms, size_t smem_
         pl.S = 1; pl.ngroups = 0; pl.rpc = (int)N;
         pl.smem = one_smem;
         pl.cache_k = kc;
+        pl.one_threads = one_threads;
         pl.seg_bytes = 0;
         pl.ws_bytes = ELA_WS_HEADER;
     } else if (chosen == ELA_PATH_GRID) {
@@ -2344,6 +2424,7 @@ int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bo
     snprintf(key, sizeof key, "%d|%d|%lld|%lld|%lld|%d|%d|%.16s|%.16s|%.16s|%.16s", dev, dtype, (long long)B,
              (long long)N, (long long)M, path, allow_cluster ? 1 : 0, knob("ELA_CTAS_PER_PROBLEM"),
              knob("ELA_CLUSTER_SIZE"), knob("ELA_CLUSTERS_PER_PROBLEM"), knob("ELA_ROW_CACHE"));
+    strncat(key, knob("ELA_WIDE_CTA"), sizeof key - strlen(key) - 1);
     {
         std::lock_guard<std::mutex> lock(g_plan_mu);
         auto it = g_plans.find(key);
@@ -2405,13 +2486,17 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
         return e == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
     if (pl.S == 1) {
-        auto kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE>;
+        const bool wide = pl.one_threads == ELA_THREADS_MULTI;
+        auto kern = wide ? auction_kernel<In, R, false, ELA_THREADS_MULTI, 1>
+                         : auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE>;
         if constexpr (std::is_same<R, float>::value)
-            if (p.cache_k > 0) kern = auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, true>;
+            if (p.cache_k > 0)
+                kern = wide ? auction_kernel<In, R, false, ELA_THREADS_MULTI, 1, true>
+                            : auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, true>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
         const int64_t grid = p.B < (1ll << 20) ? p.B : (1ll << 20);
-        kern<<<(unsigned int)grid, ELA_THREADS_ONE, pl.smem, stream>>>(p);
+        kern<<<(unsigned int)grid, pl.one_threads, pl.smem, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
     auto kern = auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI>;
