@@ -710,21 +710,35 @@ __device__ __forceinline__ void finish_bid(const Params& p, const In* row, const
 // tau, the row's exact top-2 lies in S, including every occurrence of a tied
 // maximum (all of them are above tau), so the bid equals a full scan's.
 // Otherwise the row is scanned again and S rebuilt.  One warp per row; at
-// most 32 entries, one per lane.
+// most 64 entries, lane l holding entries l and l + 32.
 
 // Top-2 of row i from its cache (exact, ties included); true if it is the
 // row's top-2 (second value above the cache's bound).
-template <typename R>
-__device__ __forceinline__ bool cache_top2(const R* __restrict__ Ps, const unsigned short* ccol, const R* ccost,
-                                           int n, R tau, int lane, Top2<R>& t) {
+template <typename R, bool TWO>
+__device__ __forceinline__ bool cache_top2_t(const R* __restrict__ Ps, const unsigned short* ccol, const R* ccost,
+                                             int n, R tau, int lane, Top2<R>& t) {
     top2_init(t);
     if (lane < n) {
         const int j = ccol[lane];
         t.v1 = sub_rn(-ccost[lane], Ps[j]);
         t.p1 = j;
     }
+    if (TWO && lane + 32 < n) {  // entries are in no column order: merge (ties keep the two smallest columns)
+        Top2<R> u;
+        top2_init(u);
+        const int j = ccol[lane + 32];
+        u.v1 = sub_rn(-ccost[lane + 32], Ps[j]);
+        u.p1 = j;
+        t = top2_merge(t, u);
+    }
     t = top2_warp(t);
     return t.v2 > tau;
+}
+template <typename R>
+__device__ __forceinline__ bool cache_top2(const R* __restrict__ Ps, const unsigned short* ccol, const R* ccost,
+                                           int n, R tau, int lane, Top2<R>& t) {
+    return n > 32 ? cache_top2_t<R, true>(Ps, ccol, ccost, n, tau, lane, t)
+                  : cache_top2_t<R, false>(Ps, ccol, ccost, n, tau, lane, t);
 }
 
 // Full scan of a row of M = NCH*32*W columns held in registers (lane l has the
@@ -1158,18 +1172,43 @@ auction_kernel(const Params p) {
                             const In* row = base + (int64_t)q * p.stride_n;
                             int j1;
                             R bid;
+#ifdef ELA_PROF
+                            const long long c0 = clock64();
+                            const int hit0 = CACHE ? 1 : 0;
+#endif
                             if constexpr (CACHE) {
                                 const KLayout LC = k_layout<R>(N, M, N, nw, kc);
-                                float fb;
-                                j1 = cached_row_bid<In>(M / (32 * Elem<In>::W), row, P, eps, lane, kc,
-                                                        reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc,
-                                                        reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc,
-                                                        reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q,
-                                                        &fb);
-                                bid = fb;
+                                const unsigned short* cc = reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc;
+                                const float* cx = reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc;
+                                // the cache hit, inline: each lane one entry, exact warp top-2
+                                const int cn = smem[LC.ccnt + q];
+                                Top2<float> tt;
+                                const bool chit =
+                                    cn >= 2 && cache_top2<float>(P, cc, cx, cn, reinterpret_cast<const float*>(smem + LC.ctau)[q], lane, tt);
+                                if (chit) {
+                                    j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
+                                    bid = add_rn(P[j1], add_rn(sub_rn(tt.v1, tt.v2), eps));
+#ifdef ELA_PROF
+                                    if (lane == 0 && blockIdx.x == 0) {
+                                        atomicAdd(&g_trace[8190][7], 1ull);
+                                        atomicAdd(&g_trace[8190][8], (unsigned long long)(clock64() + (bid == 12345.f) - c0));
+                                    }
+#endif
+                                } else {  // a miss: full scan and a new cache, out of line
+                                    float fb;
+                                    j1 = cached_row_bid<In>(M / (32 * Elem<In>::W), row, P, eps, lane, kc,
+                                                            reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc,
+                                                            reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc,
+                                                            reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q,
+                                                            &fb);
+                                    bid = fb;
+                                }
                             } else {
                                 j1 = plain_row_bid<In, R>(p, row, P, eps, lane, scr_v, scr_i, &bid);
                             }
+#ifdef ELA_PROF
+                            const long long c1 = clock64() + (bid == (R)12345 ? 1 : 0);
+#endif
                             const int prev = owner[j1];
                             __syncwarp();  // every lane has read P and owner before they change
                             if (lane == 0) {
@@ -1179,6 +1218,14 @@ auction_kernel(const Params p) {
                                 if (prev >= 0) rowcol[prev] = -1;
                             }
                             __syncwarp();
+#ifdef ELA_PROF
+                            if (lane == 0 && blockIdx.x == 0) {
+                                atomicAdd(&g_trace[8190][4], 1ull);
+                                atomicAdd(&g_trace[8190][5], (unsigned long long)(c1 - c0));
+                                atomicAdd(&g_trace[8190][6], (unsigned long long)(clock64() - c1));
+                                (void)hit0;
+                            }
+#endif
                             ++n;
                             if (prev < 0 || it + n == p.max_iter) {
                                 if (lane == 0) {
@@ -2254,7 +2301,9 @@ int cluster_fit(int cs, size_t smem) {
     return n;
 }
 
-// Row-cache entries per row on the one-CTA path: the most (32, 28, ..., 16)
+// Row-cache entries per row on the one-CTA path: the most (64, 60, ..., 16;
+// at most 32 for up to 256 rows, where a larger cache costs more to fill
+// than it saves)
 // whose shared memory still lets ELA_MINB_ONE CTAs share an SM, for fp32
 // prices and rows of 128..1024 columns that are whole 16-byte chunks per lane;
 // 0 (no cache) otherwise.  ELA_ROW_CACHE=0 turns it off (tuning knob).
@@ -2265,7 +2314,7 @@ int row_cache_k(int64_t N, int64_t M, int es, size_t smem_cta, int warps) {
         if (atoi(env) == 0) return 0;
     const int64_t per_lane = 32 * (16 / es);  // columns per 16-byte chunk slot of a warp
     if (M < ELA_SMALL_M || M % per_lane != 0 || M / per_lane > 8 || M > 65535) return 0;
-    for (int kc = 32; kc >= 16; kc -= 4)
+    for (int kc = (N > 256 ? 64 : 32); kc >= 16; kc -= 4)
         if (k_layout<R>(N, M, (int)N, warps, kc).total <= smem_cta) return kc;
     return 0;
 }
