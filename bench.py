@@ -55,9 +55,11 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the bandwidth-bound config-5 leg")
-    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4"], default=None,
+    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4", "cfg4-shard8", "cfg2", "round1"], default=None,
                     help="run one small solve for an ncu capture and exit (cfg5-small: B=2 N=M=8192 "
-                         "bf16, 256 MB > L2, max_iter 50; cfg4: the B=256 N=M=512 batch, 256 MB)")
+                         "bf16, 256 MB > L2, max_iter 50; cfg4: the B=256 N=M=512 batch, 256 MB; cfg4-shard8: "
+                         "its first 32 problems, one 8-GPU shard; cfg2: the headline solve, 64 MB; round1: the "
+                         "cfg2 matrix with max_iter 1, the full-matrix bid pass)")
     ap.add_argument("--fixed-eps", action="store_true",
                     help="reference mode: constant epsilon 1e-2 instead of the cfg2 epsilon schedule")
     return ap.parse_args()
@@ -175,6 +177,12 @@ def profile_case(args):
     torch.cuda.set_device(0)
     if args.profile_case == "cfg4":
         c, eps, mi, es = ela.workloads.cfg4().cuda(), [1e-2], 1000, 4
+    elif args.profile_case == "cfg4-shard8":
+        c, eps, mi, es = ela.workloads.cfg4()[:32].contiguous().cuda(), [1e-2], 1000, 4
+    elif args.profile_case == "cfg2":
+        c, eps, mi, es = ela.workloads.cfg2().cuda(), ela.workloads.CFG2_SCHEDULE, 1000, 4
+    elif args.profile_case == "round1":
+        c, eps, mi, es = ela.workloads.cfg2().cuda(), [1.0], 1, 4
     else:
         c, eps, mi, es = ela.workloads.cfg5(8, 8192)[:2].contiguous().cuda(), [1.0 / 8193], 50, 2
     for _ in range(2):
