@@ -101,19 +101,32 @@ def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[
     columns, so the real rows' rounds are the same.  Below 128 columns the
     tied column comes from an introselect over the whole row, whose steps
     depend on the row length, and with more dummy rows than dummy columns the
-    dummy rows bid on real columns: both solve the padded copy.
+    dummy rows bid on real columns: both solve the padded problem, whose
+    padding the kernel synthesises in its loaders (``ela_auction_solve_padded``),
+    so no padded copy is built for indices either.
     """
     is_batched = cost_matrix.ndim == 3
     if not is_batched:
         cost_matrix = cost_matrix.unsqueeze(0)
     _, N, M = cost_matrix.shape
     if auto_pad and (N % 8 != 0 or M % 8 != 0):
-        from .utils import get_pad_size, pad_input, unpad_result
+        from .utils import get_pad_size
         pn, pm = get_pad_size(N), get_pad_size(M)
-        if pm == 0 or pn > pm or M < 128:  # the padding could change a bid or a tie: solve the copy
-            padded, shape = pad_input(cost_matrix)
-            out = linear_assignment(padded, epsilon, max_iter, backend, return_indices)
-            out = unpad_result(out, shape) if return_indices else out[:, :N, :M]
+        if pm == 0 or pn > pm or M < 128:
+            # the padding could change a bid or a tie: solve the padded problem,
+            # its padding synthesised by the kernel (no padded copy)
+            if return_indices:
+                if backend not in BACKENDS:
+                    raise ValueError(f"Backend '{backend}' not available. Options: {list(BACKENDS.keys())}")
+                from .solver import _as_schedule, auction_solve_padded
+                from . import _lib
+                assign, _, _, status = auction_solve_padded(cost_matrix.detach(), _as_schedule(epsilon), int(max_iter))
+                _lib.check(int(status.item()), "auction kernel")
+                idx = assign[:, :N].clamp(min=0)
+                return idx if is_batched else idx.squeeze(0)
+            from .utils import pad_input  # differentiable one-hot: autograd needs the padded tensor
+            padded, _ = pad_input(cost_matrix)
+            out = linear_assignment(padded, epsilon, max_iter, backend, False)[:, :N, :M]
             return out if is_batched else out.squeeze(0)
     elif N % 8 != 0 or M % 8 != 0:
         raise ValueError(f"Input dimensions must be multiples of 8. Got shape {cost_matrix.shape}. "

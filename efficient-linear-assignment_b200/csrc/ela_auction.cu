@@ -377,9 +377,42 @@ struct Params {
     int max_wpr;             // most warps that share one row's scan (power of two)
     int team;                // cluster path: clusters per problem
     int tie_rule;            // ELA_TIE_*: which row wins among bids within 1e-5 of the new price
+    // virtual padding (ela_auction_solve_padded): the problem is N x M, the cost
+    // tensor holds its first Nr rows and Mr columns; the other entries are
+    // pad_c (real row x pad column, pad row x real column) or dd_c (pad row x
+    // pad column), never stored.  vpad == 0: no padding (Nr == N, Mr == M).
+    int vpad;
+    int64_t Nr, Mr;
+    double pad_c, dd_c;
     int cache_k;             // one-CTA path: row-cache entries per row (0: no cache)
     size_t team_bytes;       // cluster path: workspace bytes per team
 };
+
+// Row i of the current problem, or nullptr for a virtual padding row.
+template <typename In>
+__device__ __forceinline__ const In* row_ptr(const Params& p, const In* base, int64_t i) {
+    return (p.vpad && i >= p.Nr) ? nullptr : base + i * p.stride_n;
+}
+
+// What the row scans need of the launch parameters, passed by value: an
+// out-of-line scan given a reference to the kernel's parameters would make
+// the kernel keep a local copy of all of them.
+struct RowGeo {
+    int M, vec_ok, vpad, Mr;
+    double pad_c, dd_c;
+};
+__device__ __forceinline__ RowGeo row_geo(const Params& p) {
+    return RowGeo{(int)p.M, p.vec_ok, p.vpad, (int)p.Mr, p.pad_c, p.dd_c};
+}
+
+// Cost of column `col` of a row (scalar load; the row pointer is nullptr for a
+// padding row), with the padding blocks of ela_auction_solve_padded.
+template <typename In, typename R>
+__device__ __forceinline__ R cost_at(const RowGeo& p, const In* row, int col) {
+    if (!p.vpad) return Elem<In>::template one<R>(row + col);
+    if (row != nullptr) return col < p.Mr ? Elem<In>::template one<R>(row + col) : (R)p.pad_c;
+    return col < p.Mr ? (R)p.pad_c : (R)p.dd_c;
+}
 
 // ------------------------------------------------------------ row scanning
 // W consecutive prices from shared memory (one or two vector loads).
@@ -584,7 +617,7 @@ template <> __device__ __forceinline__ Top2<float> top2_warp_fast<float>(Top2<fl
 }
 
 template <typename In, typename R>
-__device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row, const R* __restrict__ Ps,
+__device__ __forceinline__ Top2<R> scan_row_fast(const RowGeo p, const In* row, const R* __restrict__ Ps,
                                                  int lane, int sub, int wpr) {
     const int M = (int)p.M;
     Top2<R> t;
@@ -602,7 +635,7 @@ __device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row,
         else scan_chunks_fast<In, R, ELA_UNROLL_FAST>(rv, Ps, base, stride, nchunks, t);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
-            lane_merge(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), (R)-INFINITY, col);
+            lane_merge(t, sub_rn(-cost_at<In, R>(p, row, col), Ps[col]), (R)-INFINITY, col);
     }
     return top2_warp_fast(t);
 }
@@ -612,7 +645,7 @@ __device__ __forceinline__ Top2<R> scan_row_fast(const Params& p, const In* row,
 // in a round waits one memory latency per pair instead of per row.  Each row's
 // state is the one scan_row_fast computes.  `two` is warp-uniform.
 template <typename In, typename R>
-__device__ __forceinline__ void scan_rows2_fast(const Params& p, const In* ra, const In* rb, bool two,
+__device__ __forceinline__ void scan_rows2_fast(const RowGeo p, const In* ra, const In* rb, bool two,
                                                 const R* __restrict__ Ps, int lane, Top2<R>& ta, Top2<R>& tb) {
     constexpr int W = Elem<In>::W, U = 4;
     const int nchunks = (int)p.M / W;
@@ -653,7 +686,7 @@ __device__ __forceinline__ void scan_rows2_fast(const Params& p, const In* ra, c
 // of chunks per lane, so no predicated-off batch slots are issued.  The
 // result is reduced over the warp.
 template <typename In, typename R>
-__device__ __noinline__ Top2<R> scan_row(const Params& p, const In* row, const R* __restrict__ Ps,
+__device__ __noinline__ Top2<R> scan_row(const RowGeo p, const In* row, const R* __restrict__ Ps,
                                          int lane, int sub, int wpr) {
     const int M = (int)p.M;
     Top2<R> t;
@@ -670,21 +703,21 @@ __device__ __noinline__ Top2<R> scan_row(const Params& p, const In* row, const R
         else scan_chunks<In, R, 4, true>(rv, Ps, base, stride, nchunks, t);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
-            top2_add(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), col);
+            top2_add(t, sub_rn(-cost_at<In, R>(p, row, col), Ps[col]), col);
     }
     return top2_warp(t);
 }
 
 // Column choice and bid from the row's complete top-2 (whole warp, uniform).
 template <typename In, typename R>
-__device__ __forceinline__ void finish_bid(const Params& p, const In* row, const R* __restrict__ Ps,
+__device__ __forceinline__ void finish_bid(const RowGeo p, const In* row, const R* __restrict__ Ps,
                                            const Top2<R>& t, R eps, int lane, R* scr_v, int* scr_i,
                                            int& j1_out, R& bid_out) {
     const int M = (int)p.M;
     int j1;
     if (t.v1 == t.v2 && M < ELA_SMALL_M) {
         for (int col = lane; col < M; col += 32) {
-            scr_v[col] = sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]);
+            scr_v[col] = sub_rn(-cost_at<In, R>(p, row, col), Ps[col]);
             scr_i[col] = col;
         }
         __syncwarp();
@@ -861,7 +894,7 @@ __device__ __noinline__ int cached_row_bid(int nch, const In* row, const float* 
 // maximum); returns the column, *bid_out the bid.  Out of line: it serves the
 // one-bidder chains of the one-CTA kernel, whose registers stay free.
 template <typename In, typename R>
-__device__ __noinline__ int plain_row_bid(const Params& p, const In* row, const R* __restrict__ Ps, R eps, int lane,
+__device__ __noinline__ int plain_row_bid(const RowGeo p, const In* row, const R* __restrict__ Ps, R eps, int lane,
                                           R* scr_v, int* scr_i, R* bid_out) {
     Top2<R> tt = scan_row_fast<In, R>(p, row, Ps, lane, 0, 1);
     if (p.M >= ELA_SMALL_M && tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, Ps, lane, 0, 1);
@@ -1092,6 +1125,7 @@ auction_kernel(const Params p) {
     __shared__ int s_chain;  // one-bidder rounds run by warp 0 alone
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const RowGeo pg = row_geo(p);
     const int S = MULTI ? p.S : 1;
     const int g = blockIdx.x / S, c = blockIdx.x % S;
     const int N = (int)p.N, M = (int)p.M;
@@ -1169,7 +1203,7 @@ auction_kernel(const Params p) {
                     if (warp == 0) {
                         int q = active[0], n = 0;
                         for (;;) {
-                            const In* row = base + (int64_t)q * p.stride_n;
+                            const In* row = row_ptr(p, base, q);
                             int j1;
                             R bid;
 #ifdef ELA_PROF
@@ -1204,7 +1238,7 @@ auction_kernel(const Params p) {
                                     bid = fb;
                                 }
                             } else {
-                                j1 = plain_row_bid<In, R>(p, row, P, eps, lane, scr_v, scr_i, &bid);
+                                j1 = plain_row_bid<In, R>(pg, row, P, eps, lane, scr_v, scr_i, &bid);
                             }
 #ifdef ELA_PROF
                             const long long c1 = clock64() + (bid == (R)12345 ? 1 : 0);
@@ -1269,11 +1303,11 @@ auction_kernel(const Params p) {
                 const bool exact_ok = M >= ELA_SMALL_M;
                 // a row's bid from its complete top-2: tie re-scan, column, entry
                 auto emit = [&](int k, int q, const In* row, Top2<R> tt) {
-                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, P, lane, 0, 1);
+                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
                     if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                     int j1;
                     R bid;
-                    finish_bid<In, R>(p, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
+                    finish_bid<In, R>(pg, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
                     if (lane == 0) {
                         rowbid[q] = j1;
                         if (!MULTI) { lbid[k] = bid; lrow[k] = row0 + q; lcol[k] = j1; }
@@ -1306,7 +1340,7 @@ auction_kernel(const Params p) {
                         const In* ra = base + (int64_t)(row0 + qa) * p.stride_n;
                         const In* rb = base + (int64_t)(row0 + qb) * p.stride_n;
                         Top2<R> ta, tb;
-                        scan_rows2_fast<In, R>(p, ra, rb, two, P, lane, ta, tb);
+                        scan_rows2_fast<In, R>(pg, ra, rb, two, P, lane, ta, tb);
                         emit(ka, qa, ra, ta);
                         if (two) emit(kb2, qb, rb, tb);
                     }
@@ -1316,12 +1350,12 @@ auction_kernel(const Params p) {
                     const bool has = k < K;
                     const int q = has ? active[k] : 0;
                     const int i = row0 + q;
-                    const In* row = base + (int64_t)i * p.stride_n;
+                    const In* row = row_ptr(p, base, i);
                     Top2<R> tt;
                     top2_init(tt);
                     const bool exact_first = (wpr == 1) && s_exact;  // tie-heavy rows: one exact pass
-                    if (has) tt = exact_first ? scan_row<In, R>(p, row, P, lane, 0, 1)
-                                              : scan_row_fast<In, R>(p, row, P, lane, sub, wpr);
+                    if (has) tt = exact_first ? scan_row<In, R>(pg, row, P, lane, 0, 1)
+                                              : scan_row_fast<In, R>(pg, row, P, lane, sub, wpr);
 #ifdef ELA_PROF
                     if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][8], (unsigned long long)(clock64() - pt1));
 #endif
@@ -1339,7 +1373,7 @@ auction_kernel(const Params p) {
                         if (__syncthreads_or(rowtie)) {  // also orders the wtop reads before rewrites
                             Top2<R> ex;
                             top2_init(ex);
-                            if (rowtie) ex = scan_row<In, R>(p, row, P, lane, sub, wpr);
+                            if (rowtie) ex = scan_row<In, R>(pg, row, P, lane, sub, wpr);
                             if (rowtie && lane == 0) wtop[warp] = ex;
                             __syncthreads();
                             if (rowtie && sub == 0) {
@@ -1350,7 +1384,7 @@ auction_kernel(const Params p) {
                             }
                         }
                     } else if (exact_ok && has && tt.v1 == tt.v2 && !exact_first) {
-                        tt = scan_row<In, R>(p, row, P, lane, 0, 1);
+                        tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
                     }
                     if (has && sub == 0 && lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
 #ifdef ELA_PROF
@@ -1359,7 +1393,7 @@ auction_kernel(const Params p) {
                     if (has && sub == 0) {
                         int j1;
                         R bid;
-                        finish_bid<In, R>(p, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
+                        finish_bid<In, R>(pg, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
                         if (lane == 0) {
                             rowbid[q] = j1;
                             if (!MULTI) { lbid[k] = bid; lrow[k] = i; lcol[k] = j1; }
@@ -1742,6 +1776,7 @@ auction_cluster_kernel(const Params p) {
     const int ST = TC * CS;                   // CTAs per team
     const int gi = tc * CS + rank;            // this CTA within the team
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const RowGeo pg = row_geo(p);
     const int N = (int)p.N, M = (int)p.M;
     constexpr int W = Elem<In>::W;
     const int nchunks = M / W;
@@ -2038,15 +2073,15 @@ auction_cluster_kernel(const Params p) {
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
                 if (s_exact) {  // tie-heavy rows: one exact pass
-                    tt = scan_row<In, R>(p, row, P, lane, 0, 1);
+                    tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
                 } else {
-                    tt = scan_row_fast<In, R>(p, row, P, lane, 0, 1);
-                    if (tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, P, lane, 0, 1);
+                    tt = scan_row_fast<In, R>(pg, row, P, lane, 0, 1);
+                    if (tt.v1 == tt.v2) tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
                 }
                 if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                 int j1;
                 R bid;
-                finish_bid<In, R>(p, row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
+                finish_bid<In, R>(pg, row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
                 if (lane == 0) {
                     if (TC == 1) { const int slot = rank * rpc + k; lbid[slot] = bid; lrow[slot] = (IX)i; lcol[slot] = (IX)j1; }
                     else put_entry<R>(myseg, k, t1, i, j1, bid);
@@ -2743,6 +2778,63 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
     return dispatch(dtype, p, pl, s);
 }
 
+
+// The reference's padding (pad_input, src/efficient_linear_assignment/utils.py:32-105)
+// without the padded copy: the kernel solves the (B, N', M') problem and
+// synthesises the padding blocks in its loaders.  See include/ela_auction.h.
+int ela_auction_solve_padded(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
+                             int64_t stride_b, int64_t stride_n, int multiple, const double* eps_schedule,
+                             int n_eps, int max_iter, int path, int tie_rule, int64_t* assign_out,
+                             void* prices_out, int64_t* stats_out, int32_t* status_out,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+    if (multiple < 1 || N < 1 || M < 1) return ELA_ERR_ARGUMENT;
+    const int64_t Np = (N + multiple - 1) / multiple * multiple, Mp = (M + multiple - 1) / multiple * multiple;
+    if (Np == N && Mp == M)
+        return ela_auction_solve(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, path,
+                                 tie_rule, assign_out, prices_out, stats_out, status_out, workspace, workspace_bytes,
+                                 stream);
+    if (path == ELA_PATH_CLUSTER) return ELA_ERR_UNSUPPORTED;  // the cluster kernel needs 16-byte rows
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    bool done = false;
+    int rc = check_common(dtype, B, Np, Mp, eps_schedule, n_eps, max_iter, prices_out, stats_out, status_out, s, &done);
+    if (rc != ELA_OK || done) return rc;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return ELA_ERR_ARGUMENT;
+    Params p;
+    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, tie_rule, assign_out,
+                     prices_out, stats_out, p);
+    if (rc != ELA_OK) return rc;
+    p.N = Np;
+    p.M = Mp;
+    p.Nr = N;
+    p.Mr = M;
+    p.vpad = 1;
+    p.vec_ok = 0;  // scalar loads synthesise the padding
+    // 1e9 as the input dtype holds it (fp16: +inf), as torch.full(..., 1e9, dtype) does
+    double pad = 1e9;
+    if (dtype == ELA_DTYPE_F32) pad = (double)(float)1e9;
+    else if (dtype == ELA_DTYPE_F16) pad = (double)__half2float(__float2half_rn(1e9f));
+    else if (dtype == ELA_DTYPE_BF16) pad = (double)__bfloat162float(__float2bfloat16_rn(1e9f));
+    p.pad_c = pad;
+    p.dd_c = (Np > N && Mp > M) ? 0.0 : pad;  // the padding-row x padding-column block is 0 only when both pad
+    Plan pl = {};
+    rc = make_plan(dtype, B, Np, Mp, path, pl, false);
+    if (rc != ELA_OK) return rc;
+    if (workspace_bytes < pl.ws_bytes) return ELA_ERR_ARGUMENT;
+    unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
+    p.status = status_out ? status_out : reinterpret_cast<int32_t*>(ws + 4);
+    p.ws = ws;
+    p.seg_bytes = pl.seg_bytes;
+    p.S = pl.S;
+    p.ngroups = pl.ngroups;
+    p.rows_per_cta = pl.rpc;
+    p.team = pl.team;
+    p.team_bytes = pl.team_bytes;
+    p.cache_k = 0;
+    if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
+    return dispatch(dtype, p, pl, s);
+}
 
 // Same solve as ela_auction_solve, with its scratch in g_noalloc_scratch
 // instead of a caller-supplied workspace; see include/ela_auction.h.

@@ -83,6 +83,54 @@ def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int
     return assign, prices, stats, status
 
 
+def auction_solve_padded(cost: torch.Tensor, eps: list[float], max_iter: int, path: int = 0, tie_rule: int = 0,
+                         multiple: int = 8) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Solve ``pad_input(cost, multiple)`` without building it (C ABI
+    ``ela_auction_solve_padded``): the kernel synthesises the reference's
+    padding blocks (utils.py:32-105) in its loaders.  Returns the padded
+    problem's (assignment (B,N'), prices (B,M'), stats, status) like
+    ``auction_solve``; ``assignment[:, :N]`` is what ``unpad_result`` keeps.
+    No synchronisation.
+    """
+    if cost.device.type != "cuda":
+        raise RuntimeError("ela_auction_solve_padded needs a CUDA tensor (there is no CPU path)")
+    code = DTYPE_CODE.get(cost.dtype)
+    if code is None:
+        raise TypeError(f"unsupported cost dtype {cost.dtype}")
+    if cost.dim() != 3:
+        raise ValueError("cost must be (B, N, M)")
+    if cost.stride(2) != 1:
+        cost = cost.contiguous()
+    if dev_index(cost) != torch.cuda.current_device():
+        with torch.cuda.device(cost.device):
+            return auction_solve_padded(cost, eps, max_iter, path, tie_rule, multiple)
+    lib = _lib.load()
+    B, N, M = cost.shape
+    Np, Mp = -(-N // multiple) * multiple, -(-M // multiple) * multiple
+    dev = cost.device
+    pdt = torch.float64 if code == 3 else torch.float32
+    assign = torch.empty((B, Np), dtype=torch.int64, device=dev)
+    prices = torch.empty((B, Mp), dtype=pdt, device=dev)
+    stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
+    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    ws_bytes = lib.ela_auction_workspace_bytes(code, B, Np, Mp, int(path))
+    if ws_bytes == 0:
+        _lib.check(_lib.ELA_ERR_UNSUPPORTED, f"ela_auction_workspace_bytes(B={B}, N={Np}, M={Mp}, path={path})")
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    e = (ctypes.c_double * len(eps))(*eps)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.ela_auction_solve_padded(
+        cost.data_ptr(), code, B, N, M, cost.stride(0), cost.stride(1), int(multiple), e, len(eps), int(max_iter),
+        int(path), int(tie_rule), assign.data_ptr(), prices.data_ptr(), stats.data_ptr(), status.data_ptr(),
+        ws.data_ptr(), ws_bytes, stream)
+    _lib.check(rc, "ela_auction_solve_padded")
+    return assign, prices, stats, status
+
+
+def dev_index(t: torch.Tensor) -> int:
+    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+
+
 @torch.library.custom_op("ela::auction_solve", mutates_args=())
 def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int, tie_rule: int = 0) -> Tuple[
         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:

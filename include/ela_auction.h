@@ -102,6 +102,31 @@ int ela_auction_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t
                       void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The solve of the reference's padded problem without building it.  The
+ * reference requires N and M to be multiples of 8 and pads other shapes with
+ * pad_input (src/efficient_linear_assignment/utils.py:32-105): real rows get
+ * cost 1e9 on the added columns, added rows get 1e9 on the real columns and 0
+ * on the added columns (1e9 when only rows are added), 1e9 rounded to the
+ * cost's dtype (fp16: +inf; the reference's pad_input refuses fp16 because
+ * torch.full cannot store 1e9 there).  This call solves that (B, N', M') problem, N' and M' the
+ * next multiples of `multiple`, from the unpadded (B, N, M) cost: the padding
+ * entries are synthesised by the kernel's loaders and never stored.
+ *
+ * Arguments as ela_auction_solve, with N, M, strides describing the unpadded
+ * cost; assign_out holds B*N' entries (row-major (B, N'); the caller keeps the
+ * first N of each problem, as unpad_result does), prices_out B*M'.  Size the
+ * workspace with ela_auction_workspace_bytes(dtype, B, N', M', path).  Padded
+ * shapes use the one-CTA or grid kernel (scalar loads); ELA_PATH_CLUSTER
+ * returns ELA_ERR_UNSUPPORTED.  Shapes that need no padding run
+ * ela_auction_solve unchanged.
+ */
+int ela_auction_solve_padded(const void* cost, int dtype, int64_t B, int64_t N, int64_t M,
+                             int64_t stride_b, int64_t stride_n, int multiple, const double* eps_schedule,
+                             int n_eps, int max_iter, int path, int tie_rule, int64_t* assign_out,
+                             void* prices_out, int64_t* stats_out, int32_t* status_out,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/*
  * Limit, in nanoseconds, on every device-side wait of the grid path (each
  * round's exchange of bids between the CTAs that share one problem).  A wait that
  * runs out writes ELA_ERR_TIMEOUT to *status_out and the kernel returns.
