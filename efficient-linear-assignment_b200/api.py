@@ -47,6 +47,9 @@ def _scatter_rows(out: torch.Tensor, assignment: torch.Tensor, value: float) -> 
 class AuctionIMLE(torch.autograd.Function):
     """Forward: hard assignment as a one-hot.  Backward: IMLE difference
     ``P(C + lambda*G) - P(C)`` divided by lambda (reference api.py:49-149).
+    The target solve reads ``C`` and ``G`` and forms ``C + lambda*G`` in the
+    kernel's loads (no dense target tensor) wherever the one-CTA or grid kernel
+    runs the size; otherwise it solves the built sum.
 
     Only the (B,N) assignment is saved, not the dense forward one-hot, and the
     gradient is built as one zero fill plus two sparse row scatters (+1/lambda
@@ -70,9 +73,25 @@ class AuctionIMLE(torch.autograd.Function):
     def backward(ctx, grad_output):
         cost_matrix, assignment_f = ctx.saved_tensors
         lam = ctx.imle_lambda
-        target_cost = cost_matrix + lam * grad_output
         solver = _solver(ctx.backend_name, ctx.epsilon, ctx.max_iter)
-        assignment_t, _ = solver.solve(target_cost)
+        assignment_t = None
+        if isinstance(solver, AuctionB200) and grad_output.shape == cost_matrix.shape \
+                and grad_output.dtype == cost_matrix.dtype:
+            # the target cost C + lam*G is read from the two tensors by the
+            # kernel (ela_auction_solve_sum), not built (reference api.py:106-111)
+            from .solver import _as_schedule, auction_solve_sum
+            from . import _lib
+            try:
+                a, _, _, status = auction_solve_sum(cost_matrix.detach(), grad_output.detach(), lam,
+                                                    _as_schedule(ctx.epsilon), int(ctx.max_iter), solver.path,
+                                                    solver.tie_rule)
+                _lib.check(int(status.item()), "auction kernel")
+                assignment_t = a
+            except _lib.AuctionError as e:
+                if e.status != _lib.ELA_ERR_UNSUPPORTED:
+                    raise
+        if assignment_t is None:  # sizes only the cluster kernel runs: solve the built sum
+            assignment_t, _ = solver.solve(cost_matrix + lam * grad_output)
         grad = torch.zeros_like(cost_matrix)
         _scatter_rows(grad, assignment_t, 1.0 / lam)
         _scatter_rows(grad, assignment_f, -1.0 / lam)

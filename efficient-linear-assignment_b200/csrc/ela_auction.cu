@@ -145,6 +145,89 @@ __device__ __forceinline__ uint4 ld_stream16(const void* ptr) {
     return r;
 }
 
+// ------------------------------------------------------- cost sources
+// Where the scans' cost values come from.  NoSum: the cost tensor.
+// WithSum<In>: the target cost of the IMLE backward, cost + lam * grad,
+// rounded as torch evaluates it in the input dtype (lam * grad rounded to the
+// dtype, then the sum rounded), read from the two tensors (same strides;
+// gdiff = byte distance from a cost element to the matching grad element)
+// instead of a materialised sum.
+struct NoSum {
+    __device__ __forceinline__ uint4 load(const uint4* ptr) const { return ld_stream16(ptr); }
+    template <typename In, typename R> __device__ __forceinline__ R one(const In* ptr) const {
+        return Elem<In>::template one<R>(ptr);
+    }
+};
+
+template <typename In> struct SumOps;
+template <> struct SumOps<float> {
+    static __device__ __forceinline__ unsigned int add(unsigned int c, unsigned int g, double lam) {
+        return __float_as_uint(__fadd_rn(__uint_as_float(c), __fmul_rn((float)lam, __uint_as_float(g))));
+    }
+    static __device__ __forceinline__ float one(float c, float g, double lam) { return __fadd_rn(c, __fmul_rn((float)lam, g)); }
+};
+template <> struct SumOps<double> {
+    static __device__ __forceinline__ double one(double c, double g, double lam) { return __dadd_rn(c, __dmul_rn(lam, g)); }
+};
+template <> struct SumOps<__half> {
+    static __device__ __forceinline__ float one(float c, float g, double lam) {
+        const float t = __half2float(__float2half_rn(__fmul_rn((float)lam, g)));
+        return __half2float(__float2half_rn(__fadd_rn(c, t)));
+    }
+    static __device__ __forceinline__ unsigned short add(unsigned short c, unsigned short g, double lam) {
+        __half_raw hc, hg, hr;
+        hc.x = c; hg.x = g;
+        hr = __half_raw(__float2half_rn(one(__half2float(__half(hc)), __half2float(__half(hg)), lam)));
+        return hr.x;
+    }
+};
+template <> struct SumOps<__nv_bfloat16> {
+    static __device__ __forceinline__ float bf(unsigned short h) { return __uint_as_float(((unsigned int)h) << 16); }
+    static __device__ __forceinline__ float one(float c, float g, double lam) {
+        const float t = __bfloat162float(__float2bfloat16_rn(__fmul_rn((float)lam, g)));
+        return __bfloat162float(__float2bfloat16_rn(__fadd_rn(c, t)));
+    }
+    static __device__ __forceinline__ unsigned short add(unsigned short c, unsigned short g, double lam) {
+        return (unsigned short)(__float_as_uint(one(bf(c), bf(g), lam)) >> 16);  // one() is exact in bf16
+    }
+};
+
+template <typename In> struct WithSum {
+    long long gdiff;  // bytes from a cost element to the matching grad element
+    double lam;
+    __device__ __forceinline__ uint4 load(const uint4* ptr) const {
+        const uint4 c = ld_stream16(ptr);
+        const uint4 g = ld_stream16(reinterpret_cast<const char*>(ptr) + gdiff);
+        if constexpr (std::is_same<In, float>::value) {
+            return make_uint4(SumOps<float>::add(c.x, g.x, lam), SumOps<float>::add(c.y, g.y, lam),
+                              SumOps<float>::add(c.z, g.z, lam), SumOps<float>::add(c.w, g.w, lam));
+        } else if constexpr (std::is_same<In, double>::value) {
+            const double c0 = __longlong_as_double((long long)(((unsigned long long)c.y << 32) | c.x));
+            const double c1 = __longlong_as_double((long long)(((unsigned long long)c.w << 32) | c.z));
+            const double g0 = __longlong_as_double((long long)(((unsigned long long)g.y << 32) | g.x));
+            const double g1 = __longlong_as_double((long long)(((unsigned long long)g.w << 32) | g.z));
+            const unsigned long long r0 = (unsigned long long)__double_as_longlong(SumOps<double>::one(c0, g0, lam));
+            const unsigned long long r1 = (unsigned long long)__double_as_longlong(SumOps<double>::one(c1, g1, lam));
+            return make_uint4((unsigned int)r0, (unsigned int)(r0 >> 32), (unsigned int)r1, (unsigned int)(r1 >> 32));
+        } else {
+            const unsigned int cw[4] = {c.x, c.y, c.z, c.w}, gw[4] = {g.x, g.y, g.z, g.w};
+            unsigned int r[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const unsigned int lo = SumOps<In>::add((unsigned short)(cw[k] & 0xffffu), (unsigned short)(gw[k] & 0xffffu), lam);
+                const unsigned int hi = SumOps<In>::add((unsigned short)(cw[k] >> 16), (unsigned short)(gw[k] >> 16), lam);
+                r[k] = lo | (hi << 16);
+            }
+            return make_uint4(r[0], r[1], r[2], r[3]);
+        }
+    }
+    template <typename In2, typename R> __device__ __forceinline__ R one(const In2* ptr) const {
+        const R c = Elem<In2>::template one<R>(ptr);
+        const R g = Elem<In2>::template one<R>(reinterpret_cast<const In2*>(reinterpret_cast<const char*>(ptr) + gdiff));
+        return (R)SumOps<In2>::one(c, g, lam);
+    }
+};
+
 // ------------------------------------------------------------------- top-2
 // Running top-2 over one lane's columns (visited in increasing order) plus the
 // first two columns that hold the maximum, which is what decides the column
@@ -384,6 +467,11 @@ struct Params {
     int vpad;
     int64_t Nr, Mr;
     double pad_c, dd_c;
+    // fused IMLE target (ela_auction_solve_sum): the costs are cost + lam * grad,
+    // grad at byte distance gdiff from cost with the same strides
+    int gsum;
+    long long gdiff;
+    double lam;
     int cache_k;             // one-CTA path: row-cache entries per row (0: no cache)
     size_t team_bytes;       // cluster path: workspace bytes per team
 };
@@ -404,13 +492,20 @@ struct RowGeo {
 __device__ __forceinline__ RowGeo row_geo(const Params& p) {
     return RowGeo{(int)p.M, p.vec_ok, p.vpad, (int)p.Mr, p.pad_c, p.dd_c};
 }
+// The cluster kernel's rows: no virtual padding (compile-time), two registers.
+struct PlainGeo {
+    int M, vec_ok;
+    static constexpr int vpad = 0, Mr = 0;
+    static constexpr double pad_c = 0.0, dd_c = 0.0;
+};
+__device__ __forceinline__ PlainGeo plain_geo(const Params& p) { return PlainGeo{(int)p.M, p.vec_ok}; }
 
 // Cost of column `col` of a row (scalar load; the row pointer is nullptr for a
 // padding row), with the padding blocks of ela_auction_solve_padded.
-template <typename In, typename R>
-__device__ __forceinline__ R cost_at(const RowGeo& p, const In* row, int col) {
-    if (!p.vpad) return Elem<In>::template one<R>(row + col);
-    if (row != nullptr) return col < p.Mr ? Elem<In>::template one<R>(row + col) : (R)p.pad_c;
+template <typename In, typename R, typename S = NoSum, typename G = RowGeo>
+__device__ __forceinline__ R cost_at(const G& p, const In* row, int col, const S& src = S()) {
+    if (!p.vpad) return src.template one<In, R>(row + col);
+    if (row != nullptr) return col < p.Mr ? src.template one<In, R>(row + col) : (R)p.pad_c;
     return col < p.Mr ? (R)p.pad_c : (R)p.dd_c;
 }
 
@@ -477,13 +572,13 @@ __device__ __forceinline__ void exact_chunk(const uint4& raw, const R* __restric
 // Lane-local exact top-2 over chunks base, base+stride, ... below nchunks
 // (16-byte vectors of W elements).  Whole batches of UNROLL loads run without
 // bounds predicates; the last, partial batch is predicated.
-template <typename In, typename R, int UNROLL, bool PF>
+template <typename In, typename R, int UNROLL, bool PF, typename S = NoSum>
 __device__ __forceinline__ void scan_chunks(const uint4* rv, const R* __restrict__ Ps, int base, int stride,
-                                            int nchunks, Top2<R>& t) {
+                                            int nchunks, Top2<R>& t, const S& src = S()) {
     for (; base + (UNROLL - 1) * stride < nchunks; base += stride * UNROLL) {
         uint4 raw[UNROLL];
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) raw[u] = ld_stream16(rv + base + u * stride);
+        for (int u = 0; u < UNROLL; ++u) raw[u] = src.load(rv + base + u * stride);
         prefetch_batch<UNROLL, PF>(rv, base, stride, nchunks);
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) exact_chunk<In, R>(raw[u], Ps, base + u * stride, t);
@@ -492,7 +587,7 @@ __device__ __forceinline__ void scan_chunks(const uint4* rv, const R* __restrict
         uint4 raw[UNROLL > 1 ? UNROLL - 1 : 1];
 #pragma unroll
         for (int u = 0; u < UNROLL - 1; ++u)
-            if (base + u * stride < nchunks) raw[u] = ld_stream16(rv + base + u * stride);
+            if (base + u * stride < nchunks) raw[u] = src.load(rv + base + u * stride);
 #pragma unroll
         for (int u = 0; u < UNROLL - 1; ++u)
             if (base + u * stride < nchunks) exact_chunk<In, R>(raw[u], Ps, base + u * stride, t);
@@ -555,13 +650,13 @@ __device__ __forceinline__ void fast_chunk(const uint4& raw, const R* __restrict
 
 // Chunks base, base+stride, ... below nchunks.  Whole batches of UNROLL loads
 // run without bounds predicates; the last, partial batch is predicated.
-template <typename In, typename R, int UNROLL>
+template <typename In, typename R, int UNROLL, typename S = NoSum>
 __device__ __forceinline__ void scan_chunks_fast(const uint4* rv, const R* __restrict__ Ps, int base, int stride,
-                                                 int nchunks, Top2<R>& t) {
+                                                 int nchunks, Top2<R>& t, const S& src = S()) {
     for (; base + (UNROLL - 1) * stride < nchunks; base += stride * UNROLL) {
         uint4 raw[UNROLL];
 #pragma unroll
-        for (int u = 0; u < UNROLL; ++u) raw[u] = ld_stream16(rv + base + u * stride);
+        for (int u = 0; u < UNROLL; ++u) raw[u] = src.load(rv + base + u * stride);
 #pragma unroll
         for (int u = 0; u < UNROLL; ++u) fast_chunk<In, R>(raw[u], Ps, base + u * stride, t);
     }
@@ -569,7 +664,7 @@ __device__ __forceinline__ void scan_chunks_fast(const uint4* rv, const R* __res
         uint4 raw[UNROLL > 1 ? UNROLL - 1 : 1];
 #pragma unroll
         for (int u = 0; u < UNROLL - 1; ++u)
-            if (base + u * stride < nchunks) raw[u] = ld_stream16(rv + base + u * stride);
+            if (base + u * stride < nchunks) raw[u] = src.load(rv + base + u * stride);
 #pragma unroll
         for (int u = 0; u < UNROLL - 1; ++u)
             if (base + u * stride < nchunks) fast_chunk<In, R>(raw[u], Ps, base + u * stride, t);
@@ -616,9 +711,9 @@ template <> __device__ __forceinline__ Top2<float> top2_warp_fast<float>(Top2<fl
     return r;
 }
 
-template <typename In, typename R>
-__device__ __forceinline__ Top2<R> scan_row_fast(const RowGeo p, const In* row, const R* __restrict__ Ps,
-                                                 int lane, int sub, int wpr) {
+template <typename In, typename R, typename S = NoSum, typename G = RowGeo>
+__device__ __forceinline__ Top2<R> scan_row_fast(const G p, const In* row, const R* __restrict__ Ps,
+                                                 int lane, int sub, int wpr, const S& src = S()) {
     const int M = (int)p.M;
     Top2<R> t;
     top2_init(t);
@@ -629,13 +724,13 @@ __device__ __forceinline__ Top2<R> scan_row_fast(const RowGeo p, const In* row, 
         const int per_lane = (nchunks + stride - 1) / stride;
         const uint4* rv = reinterpret_cast<const uint4*>(row);
         const int base = sub * 32 + lane;
-        if (per_lane <= 1) scan_chunks_fast<In, R, 1>(rv, Ps, base, stride, nchunks, t);
-        else if (per_lane <= 2) scan_chunks_fast<In, R, 2>(rv, Ps, base, stride, nchunks, t);
-        else if (per_lane <= 4) scan_chunks_fast<In, R, 4>(rv, Ps, base, stride, nchunks, t);
-        else scan_chunks_fast<In, R, ELA_UNROLL_FAST>(rv, Ps, base, stride, nchunks, t);
+        if (per_lane <= 1) scan_chunks_fast<In, R, 1>(rv, Ps, base, stride, nchunks, t, src);
+        else if (per_lane <= 2) scan_chunks_fast<In, R, 2>(rv, Ps, base, stride, nchunks, t, src);
+        else if (per_lane <= 4) scan_chunks_fast<In, R, 4>(rv, Ps, base, stride, nchunks, t, src);
+        else scan_chunks_fast<In, R, ELA_UNROLL_FAST>(rv, Ps, base, stride, nchunks, t, src);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
-            lane_merge(t, sub_rn(-cost_at<In, R>(p, row, col), Ps[col]), (R)-INFINITY, col);
+            lane_merge(t, sub_rn(-cost_at<In, R>(p, row, col, src), Ps[col]), (R)-INFINITY, col);
     }
     return top2_warp_fast(t);
 }
@@ -644,9 +739,10 @@ __device__ __forceinline__ Top2<R> scan_row_fast(const RowGeo p, const In* row, 
 // loads of both rows are in flight together, so a warp that owns several rows
 // in a round waits one memory latency per pair instead of per row.  Each row's
 // state is the one scan_row_fast computes.  `two` is warp-uniform.
-template <typename In, typename R>
-__device__ __forceinline__ void scan_rows2_fast(const RowGeo p, const In* ra, const In* rb, bool two,
-                                                const R* __restrict__ Ps, int lane, Top2<R>& ta, Top2<R>& tb) {
+template <typename In, typename R, typename S = NoSum, typename G = RowGeo>
+__device__ __forceinline__ void scan_rows2_fast(const G p, const In* ra, const In* rb, bool two,
+                                                const R* __restrict__ Ps, int lane, Top2<R>& ta, Top2<R>& tb,
+                                                const S& src = S()) {
     constexpr int W = Elem<In>::W, U = 4;
     const int nchunks = (int)p.M / W;
     const uint4* va = reinterpret_cast<const uint4*>(ra);
@@ -657,10 +753,10 @@ __device__ __forceinline__ void scan_rows2_fast(const RowGeo p, const In* ra, co
     for (; base + (U - 1) * 32 < nchunks; base += 32 * U) {
         uint4 a[U], b[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) a[u] = ld_stream16(va + base + u * 32);
+        for (int u = 0; u < U; ++u) a[u] = src.load(va + base + u * 32);
         if (two) {
 #pragma unroll
-            for (int u = 0; u < U; ++u) b[u] = ld_stream16(vb + base + u * 32);
+            for (int u = 0; u < U; ++u) b[u] = src.load(vb + base + u * 32);
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) fast_chunk<In, R>(a[u], Ps, base + u * 32, ta);
@@ -670,9 +766,9 @@ __device__ __forceinline__ void scan_rows2_fast(const RowGeo p, const In* ra, co
         }
     }
     for (; base < nchunks; base += 32) {
-        const uint4 a = ld_stream16(va + base);
+        const uint4 a = src.load(va + base);
         uint4 b = a;
-        if (two) b = ld_stream16(vb + base);
+        if (two) b = src.load(vb + base);
         fast_chunk<In, R>(a, Ps, base, ta);
         if (two) fast_chunk<In, R>(b, Ps, base, tb);
     }
@@ -685,8 +781,35 @@ __device__ __forceinline__ void scan_rows2_fast(const RowGeo p, const In* ra, co
 // sub*32+lane, sub*32+lane+32*wpr, ...).  The batch size follows the number
 // of chunks per lane, so no predicated-off batch slots are issued.  The
 // result is reduced over the warp.
+template <typename In, typename R, typename S = NoSum, typename G = RowGeo>
+__device__ __noinline__ Top2<R> scan_row(const G p, const In* row, const R* __restrict__ Ps,
+                                         int lane, int sub, int wpr, const S src = S()) {
+    const int M = (int)p.M;
+    Top2<R> t;
+    top2_init(t);
+    if (p.vec_ok) {
+        constexpr int W = Elem<In>::W;
+        const int nchunks = M / W;
+        const int stride = 32 * wpr;
+        const int per_lane = (nchunks + stride - 1) / stride;
+        const uint4* rv = reinterpret_cast<const uint4*>(row);
+        const int base = sub * 32 + lane;
+        if (per_lane <= 1) scan_chunks<In, R, 1, false>(rv, Ps, base, stride, nchunks, t, src);
+        else if (per_lane <= 2) scan_chunks<In, R, 2, false>(rv, Ps, base, stride, nchunks, t, src);
+        else scan_chunks<In, R, 4, true>(rv, Ps, base, stride, nchunks, t, src);
+    } else {
+        for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
+            top2_add(t, sub_rn(-cost_at<In, R>(p, row, col, src), Ps[col]), col);
+    }
+    return top2_warp(t);
+}
+
+// scan_row for the cluster kernel (no padding, no fused sum): it takes the
+// launch parameters by reference, which keeps that kernel's calls as lean as
+// they were before the padding and sum variants existed (measured: 4 % of a
+// cfg2 solve against the by-value geometry).
 template <typename In, typename R>
-__device__ __noinline__ Top2<R> scan_row(const RowGeo p, const In* row, const R* __restrict__ Ps,
+__device__ __noinline__ Top2<R> scan_row_plain(const Params& p, const In* row, const R* __restrict__ Ps,
                                          int lane, int sub, int wpr) {
     const int M = (int)p.M;
     Top2<R> t;
@@ -703,21 +826,21 @@ __device__ __noinline__ Top2<R> scan_row(const RowGeo p, const In* row, const R*
         else scan_chunks<In, R, 4, true>(rv, Ps, base, stride, nchunks, t);
     } else {
         for (int col = sub * 32 + lane; col < M; col += 32 * wpr)
-            top2_add(t, sub_rn(-cost_at<In, R>(p, row, col), Ps[col]), col);
+            top2_add(t, sub_rn(-Elem<In>::template one<R>(row + col), Ps[col]), col);
     }
     return top2_warp(t);
 }
 
 // Column choice and bid from the row's complete top-2 (whole warp, uniform).
-template <typename In, typename R>
-__device__ __forceinline__ void finish_bid(const RowGeo p, const In* row, const R* __restrict__ Ps,
+template <typename In, typename R, typename S = NoSum, typename G = RowGeo>
+__device__ __forceinline__ void finish_bid(const G p, const In* row, const R* __restrict__ Ps,
                                            const Top2<R>& t, R eps, int lane, R* scr_v, int* scr_i,
-                                           int& j1_out, R& bid_out) {
+                                           int& j1_out, R& bid_out, const S& src = S()) {
     const int M = (int)p.M;
     int j1;
     if (t.v1 == t.v2 && M < ELA_SMALL_M) {
         for (int col = lane; col < M; col += 32) {
-            scr_v[col] = sub_rn(-cost_at<In, R>(p, row, col), Ps[col]);
+            scr_v[col] = sub_rn(-cost_at<In, R>(p, row, col, src), Ps[col]);
             scr_i[col] = col;
         }
         __syncwarp();
@@ -781,14 +904,15 @@ __device__ __forceinline__ bool cache_top2(const R* __restrict__ Ps, const unsig
 // holds few enough; every lane's maximum exceeds the lowest lane maximum, so
 // that bound starts the search), then the values above tau are compacted into
 // the cache with ballots.
-template <typename In, int NCH>
+template <typename In, int NCH, typename S = NoSum>
 __device__ __noinline__ Top2<float> scan_build(const In* row, const float* __restrict__ Ps, int lane, int kc,
-                                               unsigned short* ccol, float* ccost, float* ctau, unsigned char* ccnt) {
+                                               unsigned short* ccol, float* ccost, float* ctau, unsigned char* ccnt,
+                                               const S src = S()) {
     constexpr int W = Elem<In>::W, NV = NCH * W;
     const uint4* rv = reinterpret_cast<const uint4*>(row);
     uint4 raw[NCH];
 #pragma unroll
-    for (int u = 0; u < NCH; ++u) raw[u] = ld_stream16(rv + lane + 32 * u);
+    for (int u = 0; u < NCH; ++u) raw[u] = src.load(rv + lane + 32 * u);
     float v[NV];
     Top2<float> t;
     top2_init(t);
@@ -857,10 +981,10 @@ __device__ __noinline__ Top2<float> scan_build(const In* row, const float* __res
 // row's top-2, else from a full scan that rebuilds the cache.  Rows of
 // nch * 32 16-byte chunks, nch <= 32 / W (at most 32 values per lane).
 // Returns the column bid on; *bid_out gets the bid.
-template <typename In>
+template <typename In, typename S = NoSum>
 __device__ __noinline__ int cached_row_bid(int nch, const In* row, const float* __restrict__ Ps, float eps, int lane,
                                            int kc, unsigned short* ccol, float* ccost, float* ctau,
-                                           unsigned char* ccnt, float* bid_out) {
+                                           unsigned char* ccnt, float* bid_out, const S src = S()) {
     constexpr int W = Elem<In>::W;
     Top2<float> tt;
     const int n = *ccnt;
@@ -868,20 +992,20 @@ __device__ __noinline__ int cached_row_bid(int nch, const In* row, const float* 
     if (n >= 2) hit = cache_top2<float>(Ps, ccol, ccost, n, *ctau, lane, tt);
     if (!hit) {
         switch (nch) {
-        case 1: tt = scan_build<In, 1>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
-        case 2: tt = scan_build<In, 2>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
-        case 3: tt = scan_build<In, 3>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+        case 1: tt = scan_build<In, 1, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
+        case 2: tt = scan_build<In, 2, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
+        case 3: tt = scan_build<In, 3, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
         default:
             if constexpr (W == 4) {
                 switch (nch) {
-                case 4: tt = scan_build<In, 4>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
-                case 5: tt = scan_build<In, 5>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
-                case 6: tt = scan_build<In, 6>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
-                case 7: tt = scan_build<In, 7>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
-                default: tt = scan_build<In, 8>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt); break;
+                case 4: tt = scan_build<In, 4, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
+                case 5: tt = scan_build<In, 5, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
+                case 6: tt = scan_build<In, 6, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
+                case 7: tt = scan_build<In, 7, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
+                default: tt = scan_build<In, 8, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src); break;
                 }
             } else {
-                tt = scan_build<In, 4>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt);
+                tt = scan_build<In, 4, S>(row, Ps, lane, kc, ccol, ccost, ctau, ccnt, src);
             }
         }
     }
@@ -893,13 +1017,13 @@ __device__ __noinline__ int cached_row_bid(int nch, const In* row, const float* 
 // One row's bid by one warp from a full scan (exact top-2 on a tied
 // maximum); returns the column, *bid_out the bid.  Out of line: it serves the
 // one-bidder chains of the one-CTA kernel, whose registers stay free.
-template <typename In, typename R>
-__device__ __noinline__ int plain_row_bid(const RowGeo p, const In* row, const R* __restrict__ Ps, R eps, int lane,
-                                          R* scr_v, int* scr_i, R* bid_out) {
-    Top2<R> tt = scan_row_fast<In, R>(p, row, Ps, lane, 0, 1);
-    if (p.M >= ELA_SMALL_M && tt.v1 == tt.v2) tt = scan_row<In, R>(p, row, Ps, lane, 0, 1);
+template <typename In, typename R, typename S = NoSum, typename G = RowGeo>
+__device__ __noinline__ int plain_row_bid(const G p, const In* row, const R* __restrict__ Ps, R eps, int lane,
+                                          R* scr_v, int* scr_i, R* bid_out, const S src = S()) {
+    Top2<R> tt = scan_row_fast<In, R, S>(p, row, Ps, lane, 0, 1, src);
+    if (p.M >= ELA_SMALL_M && tt.v1 == tt.v2) tt = scan_row<In, R, S>(p, row, Ps, lane, 0, 1, src);
     int j1;
-    finish_bid<In, R>(p, row, Ps, tt, eps, lane, scr_v, scr_i, j1, *bid_out);
+    finish_bid<In, R, S>(p, row, Ps, tt, eps, lane, scr_v, scr_i, j1, *bid_out, src);
     return j1;
 }
 
@@ -1110,7 +1234,7 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 //                   a round's bids go straight into the CTA's shared list.
 //   MULTI == true:  S CTAs share a problem; CTA c owns the block of rows
 //                   [c*rpc, (c+1)*rpc), rpc = ceil(N/S) (few TLB pages per CTA)
-template <typename In, typename R, bool MULTI, int THREADS, int MINB, bool CACHE = false>
+template <typename In, typename R, bool MULTI, int THREADS, int MINB, bool CACHE = false, typename S = NoSum>
 __global__ void __launch_bounds__(THREADS, MINB)
 auction_kernel(const Params p) {
     static_assert(!CACHE || (!MULTI && std::is_same<R, float>::value), "row cache: one-CTA path, fp32 prices");
@@ -1125,9 +1249,13 @@ auction_kernel(const Params p) {
     __shared__ int s_chain;  // one-bidder rounds run by warp 0 alone
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const RowGeo pg = row_geo(p);
-    const int S = MULTI ? p.S : 1;
-    const int g = blockIdx.x / S, c = blockIdx.x % S;
+    S src;  // cost source: the cost tensor, or cost + lam * grad (IMLE backward target)
+    if constexpr (!std::is_same<S, NoSum>::value) {
+        src.gdiff = p.gdiff;
+        src.lam = p.lam;
+    }
+    const int SG = MULTI ? p.S : 1;
+    const int g = blockIdx.x / SG, c = blockIdx.x % SG;
     const int N = (int)p.N, M = (int)p.M;
     const int row0 = c * p.rows_per_cta;                           // first owned row
     const int my_rows = (row0 < N) ? min(p.rows_per_cta, N - row0) : 0;
@@ -1149,7 +1277,7 @@ auction_kernel(const Params p) {
     const R tol = (R)1e-5;
 
     int* abort_flag = reinterpret_cast<int*>(p.ws);
-    unsigned char* gbase = p.ws + ELA_WS_HEADER + (size_t)g * 2 * S * p.seg_bytes;
+    unsigned char* gbase = p.ws + ELA_WS_HEADER + (size_t)g * 2 * SG * p.seg_bytes;
 
     if (tid == 0) { s_ties = 0; s_exact = 0; }
     const int nprob_step = MULTI ? p.ngroups : gridDim.x;
@@ -1230,15 +1358,15 @@ auction_kernel(const Params p) {
 #endif
                                 } else {  // a miss: full scan and a new cache, out of line
                                     float fb;
-                                    j1 = cached_row_bid<In>(M / (32 * Elem<In>::W), row, P, eps, lane, kc,
+                                    j1 = cached_row_bid<In, S>(M / (32 * Elem<In>::W), row, P, eps, lane, kc,
                                                             reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc,
                                                             reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc,
                                                             reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q,
-                                                            &fb);
+                                                            &fb, src);
                                     bid = fb;
                                 }
                             } else {
-                                j1 = plain_row_bid<In, R>(pg, row, P, eps, lane, scr_v, scr_i, &bid);
+                                j1 = plain_row_bid<In, R, S>(row_geo(p), row, P, eps, lane, scr_v, scr_i, &bid, src);
                             }
 #ifdef ELA_PROF
                             const long long c1 = clock64() + (bid == (R)12345 ? 1 : 0);
@@ -1282,7 +1410,7 @@ auction_kernel(const Params p) {
             }
             PROF_MARK(pt1);
             unsigned long long* myseg =
-                reinterpret_cast<unsigned long long*>(gbase + (size_t)((t & 1) * S + c) * p.seg_bytes);
+                reinterpret_cast<unsigned long long*>(gbase + (size_t)((t & 1) * SG + c) * p.seg_bytes);
             // ---- bids against the round-start prices.  With few rows, a row is
             //      dealt to several warps so that its scan is one memory latency.
             if (K > 0) {
@@ -1303,11 +1431,11 @@ auction_kernel(const Params p) {
                 const bool exact_ok = M >= ELA_SMALL_M;
                 // a row's bid from its complete top-2: tie re-scan, column, entry
                 auto emit = [&](int k, int q, const In* row, Top2<R> tt) {
-                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
+                    if (exact_ok && tt.v1 == tt.v2) tt = scan_row<In, R, S>(row_geo(p), row, P, lane, 0, 1, src);
                     if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                     int j1;
                     R bid;
-                    finish_bid<In, R>(pg, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
+                    finish_bid<In, R, S>(row_geo(p), row, P, tt, eps, lane, scr_v, scr_i, j1, bid, src);
                     if (lane == 0) {
                         rowbid[q] = j1;
                         if (!MULTI) { lbid[k] = bid; lrow[k] = row0 + q; lcol[k] = j1; }
@@ -1322,11 +1450,11 @@ auction_kernel(const Params p) {
                         for (int k = warp; k < K; k += nw) {
                             const int q = active[k];
                             float bid;
-                            const int j1 = cached_row_bid<In>(
+                            const int j1 = cached_row_bid<In, S>(
                                 nch, base + (int64_t)q * p.stride_n, P, eps, lane, kc,
                                 reinterpret_cast<unsigned short*>(smem + LC.ccol) + (size_t)q * kc,
                                 reinterpret_cast<float*>(smem + LC.ccost) + (size_t)q * kc,
-                                reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q, &bid);
+                                reinterpret_cast<float*>(smem + LC.ctau) + q, smem + LC.ccnt + q, &bid, src);
                             if (lane == 0) { rowbid[q] = j1; lbid[k] = bid; lrow[k] = q; lcol[k] = j1; }
                         }
                 } else {
@@ -1340,7 +1468,7 @@ auction_kernel(const Params p) {
                         const In* ra = base + (int64_t)(row0 + qa) * p.stride_n;
                         const In* rb = base + (int64_t)(row0 + qb) * p.stride_n;
                         Top2<R> ta, tb;
-                        scan_rows2_fast<In, R>(pg, ra, rb, two, P, lane, ta, tb);
+                        scan_rows2_fast<In, R, S>(row_geo(p), ra, rb, two, P, lane, ta, tb, src);
                         emit(ka, qa, ra, ta);
                         if (two) emit(kb2, qb, rb, tb);
                     }
@@ -1354,8 +1482,8 @@ auction_kernel(const Params p) {
                     Top2<R> tt;
                     top2_init(tt);
                     const bool exact_first = (wpr == 1) && s_exact;  // tie-heavy rows: one exact pass
-                    if (has) tt = exact_first ? scan_row<In, R>(pg, row, P, lane, 0, 1)
-                                              : scan_row_fast<In, R>(pg, row, P, lane, sub, wpr);
+                    if (has) tt = exact_first ? scan_row<In, R, S>(row_geo(p), row, P, lane, 0, 1, src)
+                                              : scan_row_fast<In, R, S>(row_geo(p), row, P, lane, sub, wpr, src);
 #ifdef ELA_PROF
                     if (has && lane == 0 && t < 8192) atomicMax(&g_trace[t][8], (unsigned long long)(clock64() - pt1));
 #endif
@@ -1373,7 +1501,7 @@ auction_kernel(const Params p) {
                         if (__syncthreads_or(rowtie)) {  // also orders the wtop reads before rewrites
                             Top2<R> ex;
                             top2_init(ex);
-                            if (rowtie) ex = scan_row<In, R>(pg, row, P, lane, sub, wpr);
+                            if (rowtie) ex = scan_row<In, R, S>(row_geo(p), row, P, lane, sub, wpr, src);
                             if (rowtie && lane == 0) wtop[warp] = ex;
                             __syncthreads();
                             if (rowtie && sub == 0) {
@@ -1384,7 +1512,7 @@ auction_kernel(const Params p) {
                             }
                         }
                     } else if (exact_ok && has && tt.v1 == tt.v2 && !exact_first) {
-                        tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
+                        tt = scan_row<In, R, S>(row_geo(p), row, P, lane, 0, 1, src);
                     }
                     if (has && sub == 0 && lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
 #ifdef ELA_PROF
@@ -1393,7 +1521,7 @@ auction_kernel(const Params p) {
                     if (has && sub == 0) {
                         int j1;
                         R bid;
-                        finish_bid<In, R>(pg, row, P, tt, eps, lane, scr_v, scr_i, j1, bid);
+                        finish_bid<In, R, S>(row_geo(p), row, P, tt, eps, lane, scr_v, scr_i, j1, bid, src);
                         if (lane == 0) {
                             rowbid[q] = j1;
                             if (!MULTI) { lbid[k] = bid; lrow[k] = i; lcol[k] = j1; }
@@ -1418,9 +1546,9 @@ auction_kernel(const Params p) {
                 if (tid == 0 && !(p.skip_publish && first_publish && c == 0))
                     st_relaxed_u64(myseg, ((unsigned long long)t1 << 32) | (unsigned int)K);
                 first_publish = false;
-                if (tid < S) {
+                if (tid < SG) {
                     const unsigned long long* seg =
-                        reinterpret_cast<const unsigned long long*>(gbase + (size_t)((t & 1) * S + tid) * p.seg_bytes);
+                        reinterpret_cast<const unsigned long long*>(gbase + (size_t)((t & 1) * SG + tid) * p.seg_bytes);
                     const unsigned long long t0 = globaltimer_ns();
                     unsigned int spins = 0;
                     int cntv = -1;
@@ -1468,7 +1596,7 @@ auction_kernel(const Params p) {
                 PROF_ADDALL(8, pt2b - pt2);
                 if (s_fail) return;
                 if (s_extra) {  // rounds with many bids: read the remaining entries together
-                    if (!read_extra_entries<R>(gbase + (size_t)((t & 1) * S) * p.seg_bytes, p.seg_bytes, S, s_cnt,
+                    if (!read_extra_entries<R>(gbase + (size_t)((t & 1) * SG) * p.seg_bytes, p.seg_bytes, SG, s_cnt,
                                                s_off, s_exoff, t1, lbid, lrow, lcol, abort_flag, p.status))
                         return;
                 }
@@ -1776,7 +1904,6 @@ auction_cluster_kernel(const Params p) {
     const int ST = TC * CS;                   // CTAs per team
     const int gi = tc * CS + rank;            // this CTA within the team
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const RowGeo pg = row_geo(p);
     const int N = (int)p.N, M = (int)p.M;
     constexpr int W = Elem<In>::W;
     const int nchunks = M / W;
@@ -2073,15 +2200,15 @@ auction_cluster_kernel(const Params p) {
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
                 if (s_exact) {  // tie-heavy rows: one exact pass
-                    tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
+                    tt = scan_row_plain<In, R>(p, row, P, lane, 0, 1);
                 } else {
-                    tt = scan_row_fast<In, R>(pg, row, P, lane, 0, 1);
-                    if (tt.v1 == tt.v2) tt = scan_row<In, R>(pg, row, P, lane, 0, 1);
+                    tt = scan_row_fast<In, R>(plain_geo(p), row, P, lane, 0, 1);
+                    if (tt.v1 == tt.v2) tt = scan_row_plain<In, R>(p, row, P, lane, 0, 1);
                 }
                 if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
                 int j1;
                 R bid;
-                finish_bid<In, R>(pg, row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
+                finish_bid<In, R>(plain_geo(p), row, P, tt, eps, lane, nullptr, nullptr, j1, bid);
                 if (lane == 0) {
                     if (TC == 1) { const int slot = rank * rpc + k; lbid[slot] = bid; lrow[slot] = (IX)i; lcol[slot] = (IX)j1; }
                     else put_entry<R>(myseg, k, t1, i, j1, bid);
@@ -2526,7 +2653,7 @@ int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bo
 template <typename In, typename R>
 int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
     if (pl.path == ELA_PATH_CLUSTER) {
-        if (!p.vec_ok) return ELA_ERR_UNSUPPORTED;  // rows must allow 16-byte loads
+        if (!p.vec_ok || p.gsum || p.vpad) return ELA_ERR_UNSUPPORTED;  // 16-byte rows of one tensor
         auto kern = pl.idx16 ? auction_cluster_kernel<In, R, short> : auction_cluster_kernel<In, R, int>;
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
@@ -2571,19 +2698,28 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
     }
     if (pl.S == 1) {
         const bool wide = pl.one_threads == ELA_THREADS_MULTI;
+        typedef WithSum<In> WS;
         auto kern = wide ? auction_kernel<In, R, false, ELA_THREADS_MULTI, 1>
                          : auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE>;
+        if (p.gsum)
+            kern = wide ? auction_kernel<In, R, false, ELA_THREADS_MULTI, 1, false, WS>
+                        : auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, false, WS>;
         if constexpr (std::is_same<R, float>::value)
-            if (p.cache_k > 0)
+            if (p.cache_k > 0) {
                 kern = wide ? auction_kernel<In, R, false, ELA_THREADS_MULTI, 1, true>
                             : auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, true>;
+                if (p.gsum)
+                    kern = wide ? auction_kernel<In, R, false, ELA_THREADS_MULTI, 1, true, WS>
+                                : auction_kernel<In, R, false, ELA_THREADS_ONE, ELA_MINB_ONE, true, WS>;
+            }
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
             return ELA_ERR_CUDA;
         const int64_t grid = p.B < (1ll << 20) ? p.B : (1ll << 20);
         kern<<<(unsigned int)grid, pl.one_threads, pl.smem, stream>>>(p);
         return cudaGetLastError() == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
     }
-    auto kern = auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI>;
+    auto kern = p.gsum ? auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI, false, WithSum<In>>
+                       : auction_kernel<In, R, true, ELA_THREADS_MULTI, ELA_MINB_MULTI>;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pl.smem) != cudaSuccess)
         return ELA_ERR_CUDA;
     int occ = 0;
@@ -2830,6 +2966,48 @@ int ela_auction_solve_padded(const void* cost, int dtype, int64_t B, int64_t N, 
     p.team = pl.team;
     p.team_bytes = pl.team_bytes;
     p.cache_k = 0;
+    if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
+    return dispatch(dtype, p, pl, s);
+}
+
+// The IMLE backward's target solve on cost + lam * grad without materialising
+// the sum.  See include/ela_auction.h.
+int ela_auction_solve_sum(const void* cost, const void* grad, double lam, int dtype, int64_t B, int64_t N,
+                          int64_t M, int64_t stride_b, int64_t stride_n, const double* eps_schedule, int n_eps,
+                          int max_iter, int path, int tie_rule, int64_t* assign_out, void* prices_out,
+                          int64_t* stats_out, int32_t* status_out, void* workspace, size_t workspace_bytes,
+                          void* stream) {
+    if (path == ELA_PATH_CLUSTER) return ELA_ERR_UNSUPPORTED;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    bool done = false;
+    int rc = check_common(dtype, B, N, M, eps_schedule, n_eps, max_iter, prices_out, stats_out, status_out, s, &done);
+    if (rc != ELA_OK || done) return rc;
+    if (!grad || !(lam == lam) || lam == INFINITY || lam == -INFINITY) return ELA_ERR_ARGUMENT;
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return ELA_ERR_ARGUMENT;
+    Params p;
+    rc = fill_params(cost, dtype, B, N, M, stride_b, stride_n, eps_schedule, n_eps, max_iter, tie_rule, assign_out,
+                     prices_out, stats_out, p);
+    if (rc != ELA_OK) return rc;
+    p.gsum = 1;
+    p.gdiff = (long long)(reinterpret_cast<const char*>(grad) - reinterpret_cast<const char*>(cost));
+    p.lam = lam;
+    if ((reinterpret_cast<uintptr_t>(grad) & 15u) != 0) p.vec_ok = 0;
+    Plan pl = {};
+    rc = make_plan(dtype, B, N, M, path, pl, false);
+    if (rc != ELA_OK) return rc;
+    if (workspace_bytes < pl.ws_bytes) return ELA_ERR_ARGUMENT;
+    unsigned char* ws = reinterpret_cast<unsigned char*>(workspace);
+    p.status = status_out ? status_out : reinterpret_cast<int32_t*>(ws + 4);
+    p.ws = ws;
+    p.seg_bytes = pl.seg_bytes;
+    p.S = pl.S;
+    p.ngroups = pl.ngroups;
+    p.rows_per_cta = pl.rpc;
+    p.team = pl.team;
+    p.team_bytes = pl.team_bytes;
+    p.cache_k = p.vec_ok ? pl.cache_k : 0;
     if (cudaMemsetAsync(workspace, 0, pl.ws_bytes, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;

@@ -127,6 +127,50 @@ def auction_solve_padded(cost: torch.Tensor, eps: list[float], max_iter: int, pa
     return assign, prices, stats, status
 
 
+def auction_solve_sum(cost: torch.Tensor, grad: torch.Tensor, lam: float, eps: list[float], max_iter: int,
+                      path: int = 0, tie_rule: int = 0) -> Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Solve ``cost + lam * grad`` without materialising it (C ABI
+    ``ela_auction_solve_sum``): the kernel reads both tensors and rounds the sum
+    as torch does in their dtype.  Same outputs as ``auction_solve`` on the
+    materialised sum.  Raises AuctionError(ELA_ERR_UNSUPPORTED) for sizes that
+    only the cluster kernel runs.  No synchronisation.
+    """
+    if cost.device.type != "cuda" or grad.device != cost.device:
+        raise RuntimeError("ela_auction_solve_sum needs cost and grad on one CUDA device")
+    if grad.shape != cost.shape or grad.dtype != cost.dtype:
+        raise ValueError("grad must have cost's shape and dtype")
+    code = DTYPE_CODE.get(cost.dtype)
+    if code is None:
+        raise TypeError(f"unsupported cost dtype {cost.dtype}")
+    cost, grad = cost.contiguous(), grad.contiguous()
+    if dev_index(cost) != torch.cuda.current_device():
+        with torch.cuda.device(cost.device):
+            return auction_solve_sum(cost, grad, lam, eps, max_iter, path, tie_rule)
+    lib = _lib.load()
+    B, N, M = cost.shape
+    dev = cost.device
+    pdt = torch.float64 if code == 3 else torch.float32
+    assign = torch.empty((B, N), dtype=torch.int64, device=dev)
+    prices = torch.empty((B, M), dtype=pdt, device=dev)
+    stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
+    status = torch.empty((1,), dtype=torch.int32, device=dev)
+    if B == 0 or N == 0:
+        prices.zero_(); stats.zero_(); status.zero_()
+        return assign, prices, stats, status
+    ws_bytes = lib.ela_auction_workspace_bytes(code, B, N, M, int(path))
+    if ws_bytes == 0:
+        _lib.check(_lib.ELA_ERR_UNSUPPORTED, f"ela_auction_workspace_bytes(B={B}, N={N}, M={M}, path={path})")
+    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
+    e = (ctypes.c_double * len(eps))(*eps)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    rc = lib.ela_auction_solve_sum(
+        cost.data_ptr(), grad.data_ptr(), float(lam), code, B, N, M, cost.stride(0), cost.stride(1), e, len(eps),
+        int(max_iter), int(path), int(tie_rule), assign.data_ptr(), prices.data_ptr(), stats.data_ptr(),
+        status.data_ptr(), ws.data_ptr(), ws_bytes, stream)
+    _lib.check(rc, "ela_auction_solve_sum")
+    return assign, prices, stats, status
+
+
 def dev_index(t: torch.Tensor) -> int:
     return t.device.index if t.device.index is not None else torch.cuda.current_device()
 

@@ -127,6 +127,26 @@ int ela_auction_solve_padded(const void* cost, int dtype, int64_t B, int64_t N, 
                              void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The IMLE backward's second solve without its dense input.  The reference's
+ * AuctionIMLE.backward solves the target cost `cost_matrix + lambda *
+ * grad_output` (src/efficient_linear_assignment/auction/api.py:106-111), a
+ * (B,N,M) tensor it builds first.  This call solves the same problem from the
+ * two tensors: every cost the kernel reads is cost + lam * grad, rounded as
+ * torch evaluates it in the input dtype (lam * grad rounded to the dtype,
+ * then the sum rounded), so results equal ela_auction_solve on the
+ * materialised sum.  grad has cost's dtype, shape and strides (B*stride_b
+ * layout); both device pointers.  Other arguments as ela_auction_solve.  It
+ * runs on the one-CTA and grid kernels; ELA_PATH_CLUSTER, or a size only the
+ * cluster kernel fits, returns ELA_ERR_UNSUPPORTED (the caller then solves the
+ * materialised sum).
+ */
+int ela_auction_solve_sum(const void* cost, const void* grad, double lam, int dtype, int64_t B, int64_t N,
+                          int64_t M, int64_t stride_b, int64_t stride_n, const double* eps_schedule, int n_eps,
+                          int max_iter, int path, int tie_rule, int64_t* assign_out, void* prices_out,
+                          int64_t* stats_out, int32_t* status_out, void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/*
  * Limit, in nanoseconds, on every device-side wait of the grid path (each
  * round's exchange of bids between the CTAs that share one problem).  A wait that
  * runs out writes ELA_ERR_TIMEOUT to *status_out and the kernel returns.
