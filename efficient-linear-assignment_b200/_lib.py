@@ -43,6 +43,13 @@ SIGNATURES = {
         _c.c_void_p, _c.c_void_p, _c.c_double, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64,
         _c.c_int64, _c.POINTER(_c.c_double), _c.c_int, _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p,
         _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_size_t, _c.c_void_p]),
+    "ela_auction_solve_implicit": (_c.c_int, [
+        _c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64,
+        _c.POINTER(_c.c_double), _c.c_int, _c.c_int, _c.c_int, _c.c_void_p, _c.c_void_p, _c.c_void_p,
+        _c.c_void_p, _c.c_void_p]),
+    "ela_auction_implicit_costs": (_c.c_int, [
+        _c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_void_p,
+        _c.c_void_p, _c.c_void_p]),
     "ela_auction_set_wait_limit_ns": (None, [_c.c_uint64]),
     "ela_auction_debug_skip_arrive": (None, [_c.c_int]),
 }

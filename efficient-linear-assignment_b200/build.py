@@ -33,7 +33,7 @@ def nvcc() -> str:
 
 def build(force: bool = False, verbose: bool = False) -> str:
     """Compile libela_auction.so unless it is newer than its sources."""
-    deps = [SRC, os.path.join(INCLUDE, "ela_auction.h")]
+    deps = [SRC, os.path.join(PKG_DIR, "csrc", "ela_implicit.cuh"), os.path.join(INCLUDE, "ela_auction.h")]
     if not force and os.path.exists(OUT) and all(os.path.getmtime(OUT) >= os.path.getmtime(d) for d in deps):
         return OUT
     cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-o", OUT + ".tmp", SRC]

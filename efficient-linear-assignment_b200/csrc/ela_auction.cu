@@ -2398,6 +2398,8 @@ auction_cluster_kernel(const Params p) {
 #undef ELA_CLUSTER_LEAVE
 }
 
+#include "ela_implicit.cuh"
+
 }  // namespace
 
 // ================================================================ host side
@@ -3012,6 +3014,64 @@ int ela_auction_solve_sum(const void* cost, const void* grad, double lam, int dt
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
     return dispatch(dtype, p, pl, s);
+}
+
+// Implicit low-rank costs C = Q K^T on the tensor cores (ela_implicit.cuh).
+static int implicit_launch(const void* Q, const void* Kf, int dtype, int64_t B, int64_t N, int64_t M, int64_t D,
+                           const double* eps_schedule, int n_eps, int max_iter, int tie_rule, int64_t* assign_out,
+                           float* prices_out, int64_t* stats_out, int32_t* status_out, float* cost_out,
+                           void* stream) {
+    if (dtype != ELA_DTYPE_BF16 && dtype != ELA_DTYPE_F16) return ELA_ERR_ARGUMENT;
+    if (B < 0 || N < 1 || M < ELA_SMALL_M || M > 128 * ELA_IMP_MAX_TILES || D < 16 || D > 256 || D % 16 != 0)
+        return ELA_ERR_ARGUMENT;
+    if (!Q || !Kf || !status_out || (reinterpret_cast<uintptr_t>(Q) & 15u) || (reinterpret_cast<uintptr_t>(Kf) & 15u))
+        return ELA_ERR_ARGUMENT;
+    if (tie_rule != ELA_TIE_HIGHEST_ROW && tie_rule != ELA_TIE_LOWEST_ROW) return ELA_ERR_ARGUMENT;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    ImpParams p;
+    memset(&p, 0, sizeof(p));
+    p.Q = Q; p.Kf = Kf; p.half = dtype == ELA_DTYPE_F16;
+    p.B = B; p.N = N; p.M = M; p.D = D;
+    if (!cost_out) {
+        if (n_eps < 1 || n_eps > ELA_MAX_PHASES || !eps_schedule || max_iter < 0 || !assign_out || !prices_out)
+            return ELA_ERR_ARGUMENT;
+        for (int k = 0; k < n_eps; ++k) {
+            if (!(eps_schedule[k] > 0.0) || eps_schedule[k] == INFINITY) return ELA_ERR_ARGUMENT;
+            p.eps[k] = eps_schedule[k];
+        }
+    }
+    p.n_eps = n_eps; p.max_iter = max_iter; p.tie_rule = tie_rule;
+    p.assign_out = assign_out; p.prices_out = prices_out; p.stats_out = stats_out; p.status = status_out;
+    p.cost_out = cost_out;
+    p.wait_ns = g_wait_ns;
+    int sms = 0;
+    size_t smem_max = 0, smem_sm = 0;
+    int rc = device_limits(sms, smem_max, smem_sm);
+    if (rc != ELA_OK) return rc;
+    const size_t smem = i_layout(N, M, D).total;
+    if (smem > smem_max) return ELA_ERR_UNSUPPORTED;
+    if (cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
+    if (B == 0) return ELA_OK;
+    if (cudaFuncSetAttribute(implicit_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return ELA_ERR_CUDA;
+    const int64_t grid = B < (1ll << 20) ? B : (1ll << 20);
+    implicit_kernel<<<(unsigned int)grid, ELA_IMP_THREADS, smem, s>>>(p);
+    return cudaGetLastError() == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
+}
+
+int ela_auction_solve_implicit(const void* Q, const void* K, int dtype, int64_t B, int64_t N, int64_t M, int64_t D,
+                               const double* eps_schedule, int n_eps, int max_iter, int tie_rule,
+                               int64_t* assign_out, float* prices_out, int64_t* stats_out, int32_t* status_out,
+                               void* stream) {
+    return implicit_launch(Q, K, dtype, B, N, M, D, eps_schedule, n_eps, max_iter, tie_rule, assign_out, prices_out,
+                           stats_out, status_out, nullptr, stream);
+}
+
+int ela_auction_implicit_costs(const void* Q, const void* K, int dtype, int64_t B, int64_t N, int64_t M, int64_t D,
+                               float* cost_out, int32_t* status_out, void* stream) {
+    if (!cost_out) return ELA_ERR_ARGUMENT;
+    return implicit_launch(Q, K, dtype, B, N, M, D, nullptr, 0, 0, ELA_TIE_HIGHEST_ROW, nullptr, nullptr, nullptr,
+                           status_out, cost_out, stream);
 }
 
 // Same solve as ela_auction_solve, with its scratch in g_noalloc_scratch

@@ -171,6 +171,67 @@ def auction_solve_sum(cost: torch.Tensor, grad: torch.Tensor, lam: float, eps: l
     return assign, prices, stats, status
 
 
+def _implicit_args(Q: torch.Tensor, K: torch.Tensor):
+    if Q.device.type != "cuda" or K.device != Q.device:
+        raise RuntimeError("solve_implicit needs Q and K on one CUDA device")
+    if Q.dtype != K.dtype or Q.dtype not in (torch.bfloat16, torch.float16):
+        raise TypeError("Q and K must both be bfloat16 or both float16")
+    squeeze = Q.dim() == 2
+    if squeeze:
+        Q, K = Q.unsqueeze(0), K.unsqueeze(0)
+    if Q.dim() != 3 or K.dim() != 3 or Q.shape[0] != K.shape[0] or Q.shape[2] != K.shape[2]:
+        raise ValueError("Q must be (B, N, D) and K (B, M, D)")
+    return Q.contiguous(), K.contiguous(), squeeze
+
+
+def solve_implicit(Q: torch.Tensor, K: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000,
+                   tie_rule: int = _lib.TIE_HIGHEST_ROW, check: bool = True):
+    """Auction on the implicit cost C = Q K^T (minimised), cost tiles computed
+    on the tensor cores every round and never stored (C ABI
+    ``ela_auction_solve_implicit``).  Q (B,N,D), K (B,M,D) (or unbatched),
+    bf16 or fp16, D a multiple of 16 up to 256, 128 <= M <= 512.  Returns
+    (assignment (B,N) int64 with -1 unassigned, prices (B,M) fp32, stats)."""
+    Q, K, squeeze = _implicit_args(Q, K)
+    sched = _as_schedule(epsilon)
+    B, N, D = Q.shape
+    M = K.shape[1]
+    dev = Q.device
+    with torch.cuda.device(dev):
+        lib = _lib.load()
+        assign = torch.empty((B, N), dtype=torch.int64, device=dev)
+        prices = torch.empty((B, M), dtype=torch.float32, device=dev)
+        stats = torch.zeros((B, 4), dtype=torch.int64, device=dev)
+        status = torch.empty((1,), dtype=torch.int32, device=dev)
+        e = (ctypes.c_double * len(sched))(*sched)
+        rc = lib.ela_auction_solve_implicit(Q.data_ptr(), K.data_ptr(), DTYPE_CODE[Q.dtype], B, N, M, D, e, len(sched),
+                                            int(max_iter), int(tie_rule), assign.data_ptr(), prices.data_ptr(),
+                                            stats.data_ptr(), status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc, "ela_auction_solve_implicit")
+        if check:
+            _lib.check(int(status.item()), "implicit auction kernel")
+    if squeeze:
+        return assign[0], prices[0], stats[0]
+    return assign, prices, stats
+
+
+def implicit_costs(Q: torch.Tensor, K: torch.Tensor) -> torch.Tensor:
+    """The (B,N,M) fp32 costs ``solve_implicit`` uses, written out by the same
+    tensor-core instructions (C ABI ``ela_auction_implicit_costs``)."""
+    Q, K, squeeze = _implicit_args(Q, K)
+    B, N, D = Q.shape
+    M = K.shape[1]
+    dev = Q.device
+    with torch.cuda.device(dev):
+        lib = _lib.load()
+        out = torch.empty((B, N, M), dtype=torch.float32, device=dev)
+        status = torch.empty((1,), dtype=torch.int32, device=dev)
+        rc = lib.ela_auction_implicit_costs(Q.data_ptr(), K.data_ptr(), DTYPE_CODE[Q.dtype], B, N, M, D, out.data_ptr(),
+                                            status.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc, "ela_auction_implicit_costs")
+        _lib.check(int(status.item()), "implicit costs kernel")
+    return out[0] if squeeze else out
+
+
 def dev_index(t: torch.Tensor) -> int:
     return t.device.index if t.device.index is not None else torch.cuda.current_device()
 

@@ -147,6 +147,34 @@ int ela_auction_solve_sum(const void* cost, const void* grad, double lam, int dt
                           void* stream);
 
 /*
+ * Auction on implicit low-rank costs C = Q K^T, the reference's planned
+ * solve_implicit(Q, K, ...) (optimization_plan.md:11-22): cost tiles are
+ * computed on the tensor cores (tcgen05.mma, fp32 accumulation) in every
+ * round from Q (B, N, D) and K (B, M, D), never stored.  Q and K: device,
+ * contiguous, bf16 or fp16 (dtype), 16-byte aligned; D a multiple of 16 in
+ * [16, 256]; 128 <= M <= 512.  One CTA per problem.  Minimises sum C[i][a(i)]
+ * with the reference's round (eps_schedule, max_iter, tie_rule as in
+ * ela_auction_solve).  assign_out int64[B*N] (-1 = unassigned), prices_out
+ * float[B*M], stats_out int64[B*4] or NULL, status_out int32[1] (required).
+ * Each cost value is the fp32 result of one fixed MMA instruction sequence,
+ * so the solve equals ela_auction_solve on the matrix that
+ * ela_auction_implicit_costs writes; that matrix is Q K^T up to fp32
+ * rounding of the dot products.
+ */
+int ela_auction_solve_implicit(const void* Q, const void* K, int dtype, int64_t B, int64_t N, int64_t M, int64_t D,
+                               const double* eps_schedule, int n_eps, int max_iter, int tie_rule,
+                               int64_t* assign_out, float* prices_out, int64_t* stats_out, int32_t* status_out,
+                               void* stream);
+
+/*
+ * The costs ela_auction_solve_implicit uses, written out: cost_out float
+ * [B*N*M] receives C = Q K^T computed by the same tensor-core instructions.
+ * Test and inspection aid for the implicit solve (same size limits).
+ */
+int ela_auction_implicit_costs(const void* Q, const void* K, int dtype, int64_t B, int64_t N, int64_t M, int64_t D,
+                               float* cost_out, int32_t* status_out, void* stream);
+
+/*
  * Limit, in nanoseconds, on every device-side wait of the grid path (each
  * round's exchange of bids between the CTAs that share one problem).  A wait that
  * runs out writes ELA_ERR_TIMEOUT to *status_out and the kernel returns.
