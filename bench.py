@@ -55,7 +55,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the bandwidth-bound config-5 leg")
-    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4", "cfg4-shard8", "cfg2", "round1"], default=None,
+    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4", "cfg4-shard8", "cfg2", "round1", "implicit"],
+                    default=None,
                     help="run one small solve for an ncu capture and exit (cfg5-small: B=2 N=M=8192 "
                          "bf16, 256 MB > L2, max_iter 50; cfg4: the B=256 N=M=512 batch, 256 MB; cfg4-shard8: "
                          "its first 32 problems, one 8-GPU shard; cfg2: the headline solve, 64 MB; round1: the "
@@ -175,6 +176,15 @@ def profile_case(args):
     """One warm-up and one measured solve of a small case, for ncu captures."""
     import efficient_linear_assignment_b200 as ela
     torch.cuda.set_device(0)
+    if args.profile_case == "implicit":
+        g = torch.Generator().manual_seed(3)
+        Q = torch.randn(256, 512, 16, generator=g).to(torch.bfloat16).cuda()
+        K = torch.randn(256, 512, 16, generator=g).to(torch.bfloat16).cuda()
+        for _ in range(2):
+            a, p, st = ela.solve_implicit(Q, K, 1e-2, 1000)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": "implicit", "row_bids": int(st[:, 1].sum().item())}))
+        return
     if args.profile_case == "cfg4":
         c, eps, mi, es = ela.workloads.cfg4().cuda(), [1e-2], 1000, 4
     elif args.profile_case == "cfg4-shard8":
@@ -406,6 +416,56 @@ def main():
                    "max_rounds": int(r4[2][:, 0].max().item())}
         batched["verified"] = gather_and_check(r4[0].clone(), B4, c4_all, [1e-2], 1000, oracle_at_n1=True)
 
+    # implicit low-rank costs C = Q K^T (tensor cores, no cost matrix): cfg4's
+    # shape and rank, its factors U, V as bf16 Q, K; sharded like cfg4
+    implicit = None
+    if not args.no_batched:
+        import ctypes
+        from efficient_linear_assignment_b200.sharding import shard_range
+        Bi, Ni, Di = 256, 512, 16
+        gi = torch.Generator().manual_seed(3)
+        Qa = torch.randn(Bi, Ni, Di, generator=gi).to(torch.bfloat16)
+        Ka = torch.randn(Bi, Ni, Di, generator=gi).to(torch.bfloat16)
+        lo, hi = shard_range(Bi, world, rank)
+        Qi, Ki = Qa[lo:hi].contiguous().to(dev), Ka[lo:hi].contiguous().to(dev)
+        Bl = hi - lo
+        lib = ela._lib.load()
+        io = (torch.empty((Bl, Ni), dtype=torch.int64, device=dev), torch.empty((Bl, Ni), dtype=torch.float32, device=dev),
+              torch.empty((Bl, 4), dtype=torch.int64, device=dev), torch.empty((1,), dtype=torch.int32, device=dev))
+        ei = (ctypes.c_double * 1)(1e-2)
+
+        def solve_i():
+            ela._lib.check(lib.ela_auction_solve_implicit(
+                Qi.data_ptr(), Ki.data_ptr(), 2, Bl, Ni, Ni, Di, ei, 1, 1000, 0, io[0].data_ptr(), io[1].data_ptr(),
+                io[2].data_ptr(), io[3].data_ptr(), stream.cuda_stream), "ela_auction_solve_implicit")
+            return io
+        for _ in range(args.warmup):
+            ri = solve_i()
+        torch.cuda.synchronize()
+        barrier()
+        i_ms, ri = timed(solve_i, args.steps)
+        barrier()
+        ela._lib.check(int(ri[3].item()), "implicit solve")
+        im = max_over_ranks(statistics.mean(i_ms))
+        bids_i = torch.tensor([float(ri[2][:, 1].sum().item())], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(bids_i)
+        flops = bids_i.item() * Ni * Di * 2  # one row-bid: its cost row, M dot products of length D
+        tf = flops / (im * 1e-3) / 1e12
+        peak_tf = None
+        try:
+            with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+                peak_tf = float(json.load(f)["bf16_tflops"])
+        except Exception:
+            peak_tf = 1590.0
+        implicit = {"workload": "implicit C = Q K^T: B=256 N=M=512 D=16 bf16 (seed 3), eps 1e-2; no cost matrix, "
+                                "tcgen05 cost tiles every round",
+                    "problems_per_gpu": Bl, "ms_per_step": round(im, 4), "value": round(Bi / (im * 1e-3), 2),
+                    "unit": "solves/sec", "scaling": "strong", "cost_bytes_read": 0,
+                    "roofline": {"bound": "tensor", "achieved": round(tf, 4), "peak": peak_tf, "unit": "TFLOP/s",
+                                 "frac": round(tf / peak_tf / world, 6),
+                                 "note": "round-latency bound: each round's MMA covers only its few bidders"}}
+
     # the reference's own mode on the cfg2 matrix: constant epsilon 1e-2
     fixed = None
     if not args.fixed_eps:
@@ -486,6 +546,7 @@ def main():
             "cfg3": cfg3,
             "round1": round1,
             "batched": batched,
+            "implicit": implicit,
             "cfg5": cfg5,
             "clocks": clk.summary(),
         }

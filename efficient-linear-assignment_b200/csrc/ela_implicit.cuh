@@ -265,8 +265,10 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
                         }
 #pragma unroll
                         for (int k = 0; k < 16; ++k) {
-                            const Top2<float> r = top2_warp(st[k]);
-                            if (lane == 0 && c0 + k < nb) wpart[warp * ELA_IMP_NB + c0 + k] = r;
+                            if (c0 + k < nb) {  // padding slots of the MMA's N dimension need no reduction
+                                const Top2<float> r = top2_warp(st[k]);
+                                if (lane == 0) wpart[warp * ELA_IMP_NB + c0 + k] = r;
+                            }
                         }
                     }
                     tc_fence_before();
