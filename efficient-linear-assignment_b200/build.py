@@ -31,6 +31,30 @@ def nvcc() -> str:
     raise RuntimeError("nvcc not found")
 
 
+OP_SRC = os.path.join(PKG_DIR, "csrc", "ela_torch_op.cpp")
+OP_OUT = os.path.join(PKG_DIR, "libela_torch_op.so")
+
+
+def build_op(force: bool = False) -> str:
+    """Compile the C++ torch operator (torch.ops.ela_native.auction_solve) over
+    libela_auction.so, unless it is newer than its sources."""
+    deps = [OP_SRC, OUT, os.path.join(INCLUDE, "ela_auction.h")]
+    if not force and os.path.exists(OP_OUT) and all(os.path.getmtime(OP_OUT) >= os.path.getmtime(d) for d in deps):
+        return OP_OUT
+    import torch
+    tdir = os.path.dirname(torch.__file__)
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cuda_inc = os.path.join(os.path.dirname(os.path.dirname(nvcc())), "include")
+    cmd = [os.environ.get("CXX", "g++"), "-O2", "-std=c++17", "-fPIC", "-shared", f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           "-I", os.path.join(tdir, "include"), "-I", os.path.join(tdir, "include", "torch", "csrc", "api", "include"),
+           "-I", cuda_inc, "-I", INCLUDE, OP_SRC, "-o", OP_OUT + ".tmp", "-L", PKG_DIR, "-lela_auction",
+           "-L", os.path.join(tdir, "lib"), "-lc10", "-lc10_cuda", "-ltorch_cpu", "-ltorch_cuda", "-ltorch",
+           "-Wl,-rpath,$ORIGIN"]
+    subprocess.run(cmd, check=True)
+    os.replace(OP_OUT + ".tmp", OP_OUT)
+    return OP_OUT
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
     """Compile libela_auction.so unless it is newer than its sources."""
     deps = [SRC, os.path.join(PKG_DIR, "csrc", "ela_implicit.cuh"), os.path.join(INCLUDE, "ela_auction.h")]
@@ -46,3 +70,4 @@ def build(force: bool = False, verbose: bool = False) -> str:
 
 if __name__ == "__main__":
     print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build_op(force="--force" in sys.argv))

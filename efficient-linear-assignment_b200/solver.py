@@ -5,12 +5,15 @@
 -> (assignment (B,N) int64 with -1 = unassigned, prices (B,M))``,
 src/efficient_linear_assignment/auction/api.py:7-47,56-61 and
 src/efficient_linear_assignment/auction/cpp_backend.py:18-40).  The solve is
-the ``ela::auction_solve`` custom op, whose CUDA implementation calls
-``ela_auction_solve`` through the C ABI on the current stream.
+the C++ torch operator ``torch.ops.ela_native.auction_solve``
+(csrc/ela_torch_op.cpp), which calls ``ela_auction_solve`` through the C ABI
+on the current stream.  The other entry points (padded, fused sum, implicit)
+call the C ABI through ctypes.
 """
 from __future__ import annotations
 
 import ctypes
+import os
 from typing import Sequence, Tuple, Union
 
 import torch
@@ -31,55 +34,44 @@ def _as_schedule(epsilon: EpsArg) -> list[float]:
     return sched
 
 
+_op_loaded = False
+
+
+def _native_op():
+    """torch.ops.ela_native.auction_solve, the C++ operator over the C ABI
+    (csrc/ela_torch_op.cpp, built in-tree next to libela_auction.so)."""
+    global _op_loaded
+    if not _op_loaded:
+        path = os.path.join(os.path.dirname(_lib.LIB_PATH), "libela_torch_op.so")
+        if not os.path.exists(path):
+            raise ImportError(f"{path} is missing: build it with __graft_entry__.build() (no CPU fallback exists)")
+        _lib.load()
+        torch.ops.load_library(path)
+        _op_loaded = True
+    return torch.ops.ela_native.auction_solve
+
+
 def auction_solve(cost: torch.Tensor, eps: list[float], max_iter: int, path: int, tie_rule: int = 0) -> Tuple[
         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
     """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,)).
 
+    One call of the C++ operator ``torch.ops.ela_native.auction_solve``
+    (device guard, checks, outputs from the caching allocator, one
+    ``ela_auction_solve`` on the current stream; ~20 us of host time), no
+    synchronisation: the device status word is read by the caller.  A return
+    code other than ELA_OK from the library raises AuctionError.
     tie_rule: ``_lib.TIE_HIGHEST_ROW`` (0, the reference's election) or
     ``_lib.TIE_LOWEST_ROW`` (1).
-
-    The eager implementation: outputs allocated on the cost's device, one call
-    of ``ela_auction_solve`` on the current stream (which also zeroes the status
-    word and the stats), no synchronisation.  ``auction_solve_op`` is the same
-    computation registered as a torch custom op (for torch.compile graphs).
     """
     if cost.device.type != "cuda":
         raise RuntimeError("ela::auction_solve needs a CUDA tensor (there is no CPU path)")
-    code = DTYPE_CODE.get(cost.dtype)
-    if code is None:
+    if cost.dtype not in DTYPE_CODE:
         raise TypeError(f"unsupported cost dtype {cost.dtype}")
     if cost.dim() != 3:
         raise ValueError("cost must be (B, N, M)")
-    if cost.stride(2) != 1:
-        cost = cost.contiguous()
-    lib = _lib.load()
-    B, N, M = cost.shape
-    dev = cost.device
-    pdt = torch.float64 if code == 3 else torch.float32
-    if dev.index is not None and dev.index != torch.cuda.current_device():
-        with torch.cuda.device(dev):
-            return auction_solve(cost, eps, max_iter, path, tie_rule)
-    assign = torch.empty((B, N), dtype=torch.int64, device=dev)
-    prices = torch.empty((B, M), dtype=pdt, device=dev)
-    stats = torch.empty((B, 4), dtype=torch.int64, device=dev)
-    status = torch.empty((1,), dtype=torch.int32, device=dev)
-    if B == 0 or N == 0:
-        prices.zero_()
-        stats.zero_()
-        status.zero_()
-        return assign, prices, stats, status
-    ws_bytes = lib.ela_auction_workspace_bytes(code, B, N, M, int(path))
-    if ws_bytes == 0:
-        _lib.check(_lib.ELA_ERR_UNSUPPORTED if M >= 2 else _lib.ELA_ERR_ARGUMENT,
-                   f"ela_auction_workspace_bytes(B={B}, N={N}, M={M}, path={path})")
-    ws = torch.empty((ws_bytes,), dtype=torch.uint8, device=dev)
-    e = (ctypes.c_double * len(eps))(*eps)
-    stream = torch.cuda.current_stream(dev).cuda_stream
-    rc = lib.ela_auction_solve(
-        cost.data_ptr(), code, B, N, M, cost.stride(0), cost.stride(1),
-        e, len(eps), int(max_iter), int(path), int(tie_rule), assign.data_ptr(),
-        prices.data_ptr(), stats.data_ptr(), status.data_ptr(), ws.data_ptr(), ws_bytes, stream)
-    _lib.check(rc, "ela_auction_solve")
+    assign, prices, stats, status, rc = _native_op()(cost, [float(e) for e in eps], int(max_iter), int(path),
+                                                     int(tie_rule))
+    _lib.check(int(rc), "ela_auction_solve")
     return assign, prices, stats, status
 
 
@@ -236,19 +228,32 @@ def dev_index(t: torch.Tensor) -> int:
     return t.device.index if t.device.index is not None else torch.cuda.current_device()
 
 
-@torch.library.custom_op("ela::auction_solve", mutates_args=())
 def auction_solve_op(cost: torch.Tensor, eps: list[float], max_iter: int, path: int, tie_rule: int = 0) -> Tuple[
         torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    """(B,N,M) CUDA cost -> (assignment int64 (B,N), prices (B,M), stats int64 (B,4), status int32 (1,))."""
-    return auction_solve(cost, eps, max_iter, path, tie_rule)
+    """The registered operator itself (``torch.ops.ela_native.auction_solve``),
+    for torch.compile graphs: (B,N,M) CUDA cost -> (assignment, prices, stats, status)."""
+    assign, prices, stats, status, rc = _native_op()(cost, [float(e) for e in eps], int(max_iter), int(path),
+                                                     int(tie_rule))
+    if isinstance(rc, int):  # eager call; traced graphs carry rc as a symbolic int
+        _lib.check(rc, "ela_auction_solve")
+    return assign, prices, stats, status
 
 
-@auction_solve_op.register_fake
-def _(cost, eps, max_iter, path, tie_rule=0):
-    B, N, M = cost.shape
-    pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
-    return (cost.new_empty((B, N), dtype=torch.int64), cost.new_empty((B, M), dtype=pdt),
-            cost.new_empty((B, 4), dtype=torch.int64), cost.new_empty((1,), dtype=torch.int32))
+def _register_fake():
+    try:
+        _native_op()
+    except ImportError:
+        return
+
+    @torch.library.register_fake("ela_native::auction_solve")
+    def _(cost, eps, max_iter, path, tie_rule):
+        B, N, M = cost.shape
+        pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
+        return (cost.new_empty((B, N), dtype=torch.int64), cost.new_empty((B, M), dtype=pdt),
+                cost.new_empty((B, 4), dtype=torch.int64), cost.new_empty((1,), dtype=torch.int32), 0)
+
+
+_register_fake()
 
 
 def solve(cost: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path: int = _lib.PATH_AUTO,
@@ -271,8 +276,8 @@ def solve(cost: torch.Tensor, epsilon: EpsArg = 1e-2, max_iter: int = 1000, path
     sched = _as_schedule(epsilon)
     if any(not (e > 0.0) or e == float("inf") for e in sched):
         raise ValueError("every epsilon must be finite and > 0")
-    # the custom op while torch.compile traces; the plain call (no dispatcher
-    # overhead) in eager mode
+    # the registered operator while torch.compile traces, else the eager
+    # wrapper around the same operator
     fn = auction_solve_op if torch.compiler.is_compiling() else auction_solve
     if tie_rule not in (_lib.TIE_HIGHEST_ROW, _lib.TIE_LOWEST_ROW):
         raise ValueError(f"unknown tie_rule {tie_rule}")

@@ -53,3 +53,14 @@ def test_solve_rejects_bad_arguments_without_touching_the_gpu():
     assert lib.ela_auction_solve_noalloc(one, 0, 1, 8, 8, 64, 8, eps, 1, 10, 0, 7, one, one, null, null, null) == 1
     # empty batch is a no-op
     assert lib.ela_auction_solve(null, 0, 0, 8, 8, 64, 8, eps, 1, 10, 0, 0, null, null, null, null, null, 0, null) == 0
+
+
+def test_torch_operator_library_loads_and_registers():
+    """The C++ operator over the C ABI (csrc/ela_torch_op.cpp) loads without a
+    GPU and registers torch.ops.ela_native.auction_solve."""
+    import torch
+    from efficient_linear_assignment_b200 import solver
+    op = solver._native_op()
+    assert op is torch.ops.ela_native.auction_solve
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ela.auction_solve(torch.rand(1, 8, 8), [1e-2], 10, 0)
