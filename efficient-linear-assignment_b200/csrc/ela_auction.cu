@@ -569,6 +569,10 @@ __device__ __forceinline__ void exact_chunk(const uint4& raw, const R* __restric
     }
 }
 
+#ifndef ELA_EXACT16
+#define ELA_EXACT16 1  // 16-bit costs in the cluster kernel: exact scans only (1: large rounds, 2: all rounds)
+#endif
+
 // Lane-local exact top-2 over chunks base, base+stride, ... below nchunks
 // (16-byte vectors of W elements).  Whole batches of UNROLL loads run without
 // bounds predicates; the last, partial batch is predicated.
@@ -2055,9 +2059,14 @@ auction_cluster_kernel(const Params p) {
                     Top2<R> tt;
                     top2_init(tt);
                     // the lane's chunks of the slice, loaded two at a time
-                    scan_chunks_fast<In, R, 2>(rv, P, ch0 + lane, 32, ch1, tt);
-                    tt = top2_warp_fast(tt);
-                    if (tt.p1 >= 0 && tt.v1 == tt.v2) {  // tied maximum in the slice: exact columns
+                    if (ELA_EXACT16 >= 2 && sizeof(In) == 2) {
+                        scan_chunks<In, R, 2, false>(rv, P, ch0 + lane, 32, ch1, tt);
+                        tt = top2_warp(tt);
+                    } else {
+                        scan_chunks_fast<In, R, 2>(rv, P, ch0 + lane, 32, ch1, tt);
+                        tt = top2_warp_fast(tt);
+                    }
+                    if (!(ELA_EXACT16 >= 2 && sizeof(In) == 2) && tt.p1 >= 0 && tt.v1 == tt.v2) {  // tied maximum in the slice: exact columns
                         top2_init(tt);
                         scan_chunks<In, R, 2, false>(rv, P, ch0 + lane, 32, ch1, tt);
                         tt = top2_warp(tt);
@@ -2199,7 +2208,9 @@ auction_cluster_kernel(const Params p) {
                 const int i = act[gi + k * ST];
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
-                if (s_exact) {  // tie-heavy rows: one exact pass
+                // tie-heavy rows, and 16-bit costs (whose 8-wide fast chunk costs
+                // more than the exact one's filter), take one exact pass
+                if (s_exact || (ELA_EXACT16 >= 1 && sizeof(In) == 2)) {
                     tt = scan_row_plain<In, R>(p, row, P, lane, 0, 1);
                 } else {
                     tt = scan_row_fast<In, R>(plain_geo(p), row, P, lane, 0, 1);
