@@ -1825,16 +1825,57 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int p
     }
 }
 
+// One pass over the rows (ballots kept per lane) for 16-bit costs: cfg5-like
+// solves whose late rounds have a few hundred bidders among 8192 rows spend
+// half the cycles of the two-pass walk there (-3 % of the solve).  The fp32
+// instance keeps the two-pass walk: with the one-pass code the 4096^2 fp32
+// epsilon-schedule solve measured 3 % slower (code generation of its
+// small-round loop, not the compaction itself, which runs ~50 times a solve).
+#ifndef ELA_ONEPASS_COMPACT
+#define ELA_ONEPASS_COMPACT(In) (sizeof(In) == 2)
+#endif
+
 // Block-wide ordered compaction of the rows with rowcol < 0 into act[];
 // returns the count (all threads).  Deterministic: ascending row order.
-template <typename IX>
+template <typename IX, bool ONEPASS>
 __device__ int compact_unassigned(const IX* rowcol, int N, IX* act, int* s_scan) {
     // Each warp owns a contiguous block of rows (a multiple of 32) and walks it
     // 32 rows at a time: consecutive lanes read consecutive entries (no bank
-    // conflicts) and a ballot gives the count and each row's slot.
+    // conflicts) and a ballot marks the unassigned rows.  Up to 32 ballots per
+    // warp, lane k keeps the k-th, so the rows are read once; a warp scan of
+    // the lanes' counts and the warps' totals place each lane's rows.
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int per = (((N + nw - 1) / nw) + 31) & ~31;
     const int r0 = warp * per, r1 = min(N, r0 + per);
+    if (ONEPASS && per <= 32 * 32) {
+        unsigned int mine = 0u;
+        int k = 0;
+#pragma unroll 4
+        for (int b = r0; b < r1; b += 32, ++k) {
+            const int i = b + lane;
+            const unsigned int m = __ballot_sync(0xffffffffu, i < r1 && rowcol[i] < 0);
+            mine = (lane == k) ? m : mine;
+        }
+        const int c = __popc(mine);
+        int incl = c;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) s_scan[warp] = incl;
+        __syncthreads();
+        const unsigned int w = (lane < nw) ? (unsigned int)s_scan[lane] : 0u;
+        int pos = (int)__reduce_add_sync(0xffffffffu, lane < warp ? w : 0u) + incl - c;
+        const int total = (int)__reduce_add_sync(0xffffffffu, w);
+        const int rb = r0 + 32 * lane;
+        while (mine) {
+            act[pos++] = (IX)(rb + __ffs(mine) - 1);
+            mine &= mine - 1u;
+        }
+        __syncthreads();
+        return total;
+    }
     int cnt = 0;
     for (int b = r0; b < r1; b += 32) {
         const int i = b + lane;
@@ -1974,7 +2015,7 @@ auction_cluster_kernel(const Params p) {
         int ph = 0, it = 0;
         R eps = (R)p.eps[0];  // this epsilon (read once per epsilon)
         __syncthreads();
-        int K = compact_unassigned(rowcol, N, act, s_scan);  // rows that bid this round, ascending
+        int K = compact_unassigned<IX, ELA_ONEPASS_COMPACT(In)>(rowcol, N, act, s_scan);  // rows that bid this round, ascending
         bool small = small_ok && K <= ELA_SMALL_ROUND;
 #ifdef ELA_PROF
         long long lastS5 = 0;
@@ -2027,7 +2068,7 @@ auction_cluster_kernel(const Params p) {
                 for (int j = tid; j < M; j += blockDim.x) owner[j] = (IX)-1;
                 for (int i = tid; i < N; i += blockDim.x) rowcol[i] = (IX)-1;
                 __syncthreads();
-                K = compact_unassigned(rowcol, N, act, s_scan);
+                K = compact_unassigned<IX, ELA_ONEPASS_COMPACT(In)>(rowcol, N, act, s_scan);
                 small = small_ok && K <= ELA_SMALL_ROUND;
 #ifdef ELA_PROF
                 if (b == 0 && leader && rank == 0 && tid == 0) {
@@ -2353,7 +2394,7 @@ auction_cluster_kernel(const Params p) {
             PROF_MARK(L3);
             ++it;
             // ---- next round's bidders (ascending); few -> small rounds
-            K = compact_unassigned(rowcol, N, act, s_scan);
+            K = compact_unassigned<IX, ELA_ONEPASS_COMPACT(In)>(rowcol, N, act, s_scan);
             if (small_ok && K <= ELA_SMALL_ROUND) small = true;
             PROF_MARK(L4);
 #ifdef ELA_PROF
@@ -2369,6 +2410,10 @@ auction_cluster_kernel(const Params p) {
                 g_trace[it - 1][0] = nent; g_trace[it - 1][1] = L1 - L0; g_trace[it - 1][2] = L2 - L1;
                 g_trace[it - 1][3] = L3 - L2; g_trace[it - 1][4] = L4 - L3; g_trace[it - 1][5] = Kl;
                 g_trace[it - 1][6] = 1;
+            }
+            if (b == 0 && tid == 0 && it - 1 < 8192) {  // slowest CTA of problem 0: own scan, scan + exchange
+                atomicMax(&g_trace[it - 1][7], (unsigned long long)(L1 - L0));
+                atomicMax(&g_trace[it - 1][8], (unsigned long long)(L2 - L0));
             }
 #endif
         }
