@@ -1835,6 +1835,32 @@ __device__ __forceinline__ bool mbar_wait(unsigned long long* mb, unsigned int p
 #define ELA_ONEPASS_COMPACT(In) (sizeof(In) == 2)
 #endif
 
+#ifndef ELA_SPLIT_LARGE
+#define ELA_SPLIT_LARGE 1  // 16-bit costs, large rounds with at most nw/2 rows per CTA: several warps per row
+#endif
+
+// Large rounds with few rows per CTA: warp w's share of row act[(w / wpr) * ST]
+// (chunks strided over the row's wpr warps), top-2 into part[w]: exact
+// (ties included) from one exact pass, or from the fast pass with an exact
+// re-scan of a share whose maximum is tied.  Used for 16-bit costs only: in
+// the fp32 cluster kernel the extra code spilled registers and cost the
+// 4096^2 solve 17 %.
+template <typename In, typename R, typename IX>
+__device__ __forceinline__ void large_share(const PlainGeo g, int64_t stride_n, const In* base, const IX* act, int ST,
+                                         int wpr, bool exact, const R* __restrict__ P, Top2<R>* part) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int kr = warp / wpr, sub = warp - kr * wpr;
+    const In* row = base + (int64_t)act[kr * ST] * stride_n;
+    Top2<R> tt;
+    if (exact) {
+        tt = scan_row<In, R, NoSum, PlainGeo>(g, row, P, lane, sub, wpr);
+    } else {
+        tt = scan_row_fast<In, R>(g, row, P, lane, sub, wpr);
+        if (tt.p1 >= 0 && tt.v1 == tt.v2) tt = scan_row<In, R, NoSum, PlainGeo>(g, row, P, lane, sub, wpr);
+    }
+    if (lane == 0) part[warp] = tt;
+}
+
 // Block-wide ordered compaction of the rows with rowcol < 0 into act[];
 // returns the count (all threads).  Deterministic: ascending row order.
 template <typename IX, bool ONEPASS>
@@ -2245,7 +2271,33 @@ auction_cluster_kernel(const Params p) {
             const unsigned int t1 = t + 1;
             unsigned long long* myseg =
                 reinterpret_cast<unsigned long long*>(tb + (size_t)((t & 1) * ST + gi) * p.seg_bytes);
-            for (int k = warp; k < Kl; k += nw) {  // one warp per row
+            const int wprl = (ELA_SPLIT_LARGE && sizeof(In) == 2 && Kl > 0 && 2 * Kl <= nw) ? nw / Kl : 1;
+            if (wprl > 1) {
+                // few rows: each row's chunks dealt to wprl warps, the exact
+                // partials merged in shared memory (no small-round data is in
+                // flight in a large round, so the partial buffer is free)
+                if (warp < Kl * wprl)
+                    large_share<In, R, IX>(plain_geo(p), p.stride_n, base, act + gi, ST, wprl,
+                                           s_exact || (ELA_EXACT16 >= 1 && sizeof(In) == 2), P, part);
+                __syncthreads();
+            }
+            for (int k = warp; k < Kl && wprl > 1; k += nw) {  // row k from its wprl partials
+                const int i = act[gi + k * ST];
+                Top2<R> tt;
+                top2_init(tt);
+                if (lane < wprl) tt = part[k * wprl + lane];
+                tt = top2_warp(tt);
+                if (lane == 0 && tt.v1 == tt.v2) atomicAdd(&s_ties, 1);
+                int j1;
+                R bid;
+                finish_bid<In, R>(plain_geo(p), base + (int64_t)i * p.stride_n, P, tt, eps, lane, nullptr, nullptr, j1,
+                                  bid);
+                if (lane == 0) {
+                    if (TC == 1) { const int slot = rank * rpc + k; lbid[slot] = bid; lrow[slot] = (IX)i; lcol[slot] = (IX)j1; }
+                    else put_entry<R>(myseg, k, t1, i, j1, bid);
+                }
+            }
+            for (int k = warp; k < Kl && wprl == 1; k += nw) {  // one warp per row
                 const int i = act[gi + k * ST];
                 const In* row = base + (int64_t)i * p.stride_n;
                 Top2<R> tt;
