@@ -1228,6 +1228,9 @@ __host__ __device__ inline KLayout k_layout(int64_t N, int64_t M, int rpc, int w
 #define ELA_MINB_ONE 2
 #endif
 #define ELA_THREADS_MULTI 512
+#ifndef ELA_THREADS_CLUSTER
+#define ELA_THREADS_CLUSTER 512  // threads per CTA of the cluster kernel
+#endif
 #define ELA_MINB_MULTI 1
 #define ELA_MAX_S 256
 #define ELA_WS_HEADER 256
@@ -1948,7 +1951,7 @@ __device__ __noinline__ void cluster_leave(int* abort_flag, bool pending, int* s
 // the end of the epsilon and then reload the prices the leader publishes.
 // Per-team workspace: [2 x ST exchange segments][prices M][flag word].
 template <typename In, typename R, typename IX>
-__global__ void __launch_bounds__(ELA_THREADS_MULTI, 1)
+__global__ void __launch_bounds__(ELA_THREADS_CLUSTER, 1)
 auction_cluster_kernel(const Params p) {
     namespace cg = cooperative_groups;
     typedef Bits<R> BT;
@@ -2566,7 +2569,7 @@ int cluster_fit(int cs, size_t smem) {
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cs; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
-    cfg.gridDim = dim3(cs); cfg.blockDim = dim3(ELA_THREADS_MULTI); cfg.dynamicSmemBytes = smem;
+    cfg.gridDim = dim3(cs); cfg.blockDim = dim3(ELA_THREADS_CLUSTER); cfg.dynamicSmemBytes = smem;
     cfg.attrs = attr; cfg.numAttrs = 1;
     int n = 0;
     if (cudaOccupancyMaxActiveClusters(&n, (void*)kern, &cfg) != cudaSuccess) { cudaGetLastError(); return 0; }
@@ -2776,7 +2779,7 @@ int launch(const Params& p, const Plan& pl, cudaStream_t stream) {
         attr[1].id = cudaLaunchAttributeCooperative;
         attr[1].val.cooperative = 1;
         cfg.gridDim = dim3(pl.cs * pl.nclusters);
-        cfg.blockDim = dim3(ELA_THREADS_MULTI);
+        cfg.blockDim = dim3(ELA_THREADS_CLUSTER);
         cfg.dynamicSmemBytes = pl.smem;
         cfg.stream = stream;
         cfg.attrs = attr;
