@@ -47,7 +47,12 @@ struct ImpParams {
 // Shared-memory layout of the implicit kernel (bytes).
 struct ILayout {
     size_t ks, qs, P, maxb, win, owner, rowcol, act, lbid, lrow, lcol, wpart, total;
+    int kc;  // row-cache entries per row (0: no cache)
+    size_t ccol, ccost, ctau, ccnt, mrow, ment, scr;
 };
+#define ELA_IMP_KC 16          // row-cache entries per row
+#define ELA_IMP_SCR 8          // bidder rows of costs staged in shared memory per cache build
+#define ELA_IMP_SMEM_2CTA 115000  // dynamic shared memory that still lets two CTAs share an SM
 __host__ __device__ inline ILayout i_layout(int64_t N, int64_t M, int64_t D) {
     ILayout L;
     const int64_t T = (M + 127) / 128;
@@ -65,7 +70,50 @@ __host__ __device__ inline ILayout i_layout(int64_t N, int64_t M, int64_t D) {
     L.lcol = o;   o = align_up(o + 4 * (size_t)N, 16);
     L.wpart = o;  o = align_up(o + sizeof(Top2<float>) * 4 * ELA_IMP_NB, 16);
     L.total = o;
+    // row cache (M a multiple of 128, at most 512 columns): kept only while
+    // two CTAs still fit on an SM
+    L.kc = 0;
+    L.ccol = L.ccost = L.ctau = L.ccnt = L.mrow = L.ment = L.scr = 0;
+    if (M % 128 == 0 && M <= 512) {
+        const int kc = ELA_IMP_KC;
+        L.ccol = o;  o = align_up(o + 2 * (size_t)N * kc, 16);  // cached columns
+        L.ccost = o; o = align_up(o + 4 * (size_t)N * kc, 16);  // their costs
+        L.ctau = o;  o = align_up(o + 4 * (size_t)N, 16);       // bound of every other column's value
+        L.ccnt = o;  o = align_up(o + (size_t)N, 16);           // entries (0: none)
+        L.mrow = o;  o = align_up(o + 4 * (size_t)N, 16);       // this round's cache misses: row,
+        L.ment = o;  o = align_up(o + 4 * (size_t)N, 16);       //   and its bid entry
+        L.scr = o;   o = align_up(o + 4 * (size_t)ELA_IMP_SCR * M, 16);  // staged cost rows
+        if (o <= ELA_IMP_SMEM_2CTA) { L.kc = kc; L.total = o; }
+    }
     return L;
+}
+
+// Cost rows staged in shared memory, read by the cache build's scan.
+struct SharedRow {
+    __device__ __forceinline__ uint4 load(const uint4* ptr) const { return *ptr; }
+};
+
+// 8 consecutive TMEM columns of this thread's lane.
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, float* v) {
+    uint32_t r[8];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int k = 0; k < 8; ++k) v[k] = __uint_as_float(r[k]);
+}
+
+// Cache build of one staged cost row (M = 128 * nch columns): exact top-2 and
+// a new cache for the row.
+__device__ __forceinline__ Top2<float> imp_build(int nch, const float* row, const float* P, int lane, int kc,
+                                                 unsigned short* ccol, float* ccost, float* ctau, unsigned char* ccnt) {
+    switch (nch) {
+    case 1: return scan_build<float, 1, SharedRow>(row, P, lane, kc, ccol, ccost, ctau, ccnt, SharedRow());
+    case 2: return scan_build<float, 2, SharedRow>(row, P, lane, kc, ccol, ccost, ctau, ccnt, SharedRow());
+    case 3: return scan_build<float, 3, SharedRow>(row, P, lane, kc, ccol, ccost, ctau, ccnt, SharedRow());
+    default: return scan_build<float, 4, SharedRow>(row, P, lane, kc, ccol, ccost, ctau, ccnt, SharedRow());
+    }
 }
 
 // Byte offset of element (r, k) of a K-major operand tile with D columns in the
@@ -157,7 +205,7 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
     extern __shared__ __align__(128) unsigned char smem[];
     __shared__ __align__(8) unsigned long long s_mbar;
     __shared__ uint32_t s_tmem;
-    __shared__ int s_nact, s_fail;
+    __shared__ int s_nact, s_fail, s_nmiss;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int N = (int)p.N, M = (int)p.M, D = (int)p.D;
     const int T = (M + 127) / 128;
@@ -172,6 +220,14 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
     int* lrow = reinterpret_cast<int*>(smem + L.lrow);
     int* lcol = reinterpret_cast<int*>(smem + L.lcol);
     Top2<float>* wpart = reinterpret_cast<Top2<float>*>(smem + L.wpart);
+    const int kc = L.kc;
+    unsigned short* ccol = reinterpret_cast<unsigned short*>(smem + L.ccol);
+    float* ccost = reinterpret_cast<float*>(smem + L.ccost);
+    float* ctau = reinterpret_cast<float*>(smem + L.ctau);
+    unsigned char* ccnt = smem + L.ccnt;
+    int* mrow = reinterpret_cast<int*>(smem + L.mrow);
+    int* ment = reinterpret_cast<int*>(smem + L.ment);
+    float* scr = reinterpret_cast<float*>(smem + L.scr);
     const float tol = 1e-5f;
 
     if (warp == 0) {  // TMEM columns for the accumulators, held until exit
@@ -203,6 +259,8 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
         }
         for (int j = tid; j < M; j += blockDim.x) { P[j] = 0.f; maxb[j] = 0u; win[j] = 0; owner[j] = -1; }
         for (int i = tid; i < N; i += blockDim.x) rowcol[i] = -1;
+        if (kc > 0)
+            for (int i = tid; i < N; i += blockDim.x) ccnt[i] = 0;
         __syncthreads();
 
         if (p.cost_out) {  // materialise the costs with the same MMA sequence
@@ -242,8 +300,68 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
                 __syncthreads();
                 const int K = s_nact;
                 if (K == 0) break;
-                // ---- bids, ELA_IMP_NB rows per MMA pass
-                for (int k0 = 0; k0 < K; k0 += ELA_IMP_NB) {
+                if (kc > 0) {
+                    // ---- bids from the row caches (prices never fall, so a
+                    //      cache whose second value is above its bound holds the
+                    //      row's exact top-2); the misses go through the MMA
+                    if (tid == 0) s_nmiss = 0;
+                    __syncthreads();
+                    for (int k = warp; k < K; k += ELA_IMP_THREADS / 32) {
+                        const int i = act[k], n = ccnt[i];
+                        Top2<float> tt;
+                        const bool hit = n >= 2 && cache_top2<float>(P, ccol + (size_t)i * kc, ccost + (size_t)i * kc,
+                                                                      n, ctau[i], lane, tt);
+                        if (lane == 0) {
+                            if (hit) {
+                                const int j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
+                                lbid[k] = add_rn(P[j1], add_rn(sub_rn(tt.v1, tt.v2), eps));
+                                lrow[k] = i;
+                                lcol[k] = j1;
+                            } else {
+                                const int m = atomicAdd(&s_nmiss, 1);
+                                mrow[m] = i;
+                                ment[m] = k;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    const int nm = s_nmiss;
+                    for (int m0 = 0; m0 < nm; m0 += ELA_IMP_NB) {
+                        const int nb = min(ELA_IMP_NB, nm - m0), npad = (nb + 15) & ~15;
+                        if (!imp_mma_pass(p, Qb, nb, mrow + m0, smem, L, tmem, &s_mbar, phase, T, npad, &s_fail)) {
+                            failed = true;
+                            break;
+                        }
+                        for (int c0 = 0; c0 < nb; c0 += ELA_IMP_SCR) {
+                            // stage ELA_IMP_SCR rows of costs (lane = column), then
+                            // one warp per row: exact top-2, bid, new cache
+                            for (int t = 0; t < T; ++t) {
+                                float v[ELA_IMP_SCR];
+                                tc_ld8(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(t * ELA_IMP_NB + c0), v);
+                                const int j = t * 128 + 32 * warp + lane;
+#pragma unroll
+                                for (int k = 0; k < ELA_IMP_SCR; ++k) scr[k * M + j] = v[k];
+                            }
+                            __syncthreads();
+                            for (int k = warp; k < ELA_IMP_SCR && c0 + k < nb; k += ELA_IMP_THREADS / 32) {
+                                const int m = m0 + c0 + k, i = mrow[m], e = ment[m];
+                                const Top2<float> tt = imp_build(T, scr + k * M, P, lane, kc, ccol + (size_t)i * kc,
+                                                                 ccost + (size_t)i * kc, ctau + i, ccnt + i);
+                                if (lane == 0) {
+                                    const int j1 = (tt.p2 >= 0 && !(tt.p1 == 0 && tt.p2 == 1)) ? tt.p2 : tt.p1;
+                                    lbid[e] = add_rn(P[j1], add_rn(sub_rn(tt.v1, tt.v2), eps));
+                                    lrow[e] = i;
+                                    lcol[e] = j1;
+                                }
+                            }
+                            __syncthreads();  // the staged rows are read before the next ones land
+                        }
+                        tc_fence_before();
+                        __syncthreads();
+                    }
+                }
+                // ---- bids, ELA_IMP_NB rows per MMA pass (no row cache)
+                for (int k0 = 0; k0 < K && kc == 0; k0 += ELA_IMP_NB) {
                     const int nb = min(ELA_IMP_NB, K - k0), npad = (nb + 15) & ~15;
                     if (!imp_mma_pass(p, Qb, nb, act + k0, smem, L, tmem, &s_mbar, phase, T, npad, &s_fail)) {
                         failed = true;
