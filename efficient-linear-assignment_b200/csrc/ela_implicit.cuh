@@ -46,7 +46,7 @@ struct ImpParams {
 
 // Shared-memory layout of the implicit kernel (bytes).
 struct ILayout {
-    size_t ks, qs, P, maxb, win, owner, rowcol, act, lbid, lrow, lcol, wpart, total;
+    size_t ks, qs, P, win, owner, rowcol, act, lbid, lrow, lcol, wpart, total;
     int kc;  // row-cache entries per row (0: no cache)
     size_t ccol, ccost, ctau, ccnt, mrow, ment, scr;
 };
@@ -60,7 +60,6 @@ __host__ __device__ inline ILayout i_layout(int64_t N, int64_t M, int64_t D) {
     L.ks = o;     o = align_up(o + (size_t)(T * 128) * D * 2, 128);       // K factor, core-matrix layout
     L.qs = o;     o = align_up(o + (size_t)ELA_IMP_NB * D * 2, 128);      // the bidders' Q rows
     L.P = o;      o = align_up(o + 4 * (size_t)M, 16);
-    L.maxb = o;   o = align_up(o + 4 * (size_t)M, 16);
     L.win = o;    o = align_up(o + 4 * (size_t)M, 16);
     L.owner = o;  o = align_up(o + 4 * (size_t)M, 16);
     L.rowcol = o; o = align_up(o + 4 * (size_t)N, 16);
@@ -211,7 +210,7 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
     const int T = (M + 127) / 128;
     const ILayout L = i_layout(N, M, D);
     float* P = reinterpret_cast<float*>(smem + L.P);
-    unsigned int* maxb = reinterpret_cast<unsigned int*>(smem + L.maxb);
+    unsigned int* Pbits = reinterpret_cast<unsigned int*>(smem + L.P);  // prices >= 0: bit order is value order
     int* win = reinterpret_cast<int*>(smem + L.win);
     int* owner = reinterpret_cast<int*>(smem + L.owner);
     int* rowcol = reinterpret_cast<int*>(smem + L.rowcol);
@@ -257,7 +256,8 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
             if (r < M) v = *reinterpret_cast<const uint4*>(Kb + (size_t)r * D + kc * 8);
             *reinterpret_cast<uint4*>(smem + L.ks + core_off(r, kc * 8, D)) = v;
         }
-        for (int j = tid; j < M; j += blockDim.x) { P[j] = 0.f; maxb[j] = 0u; win[j] = 0; owner[j] = -1; }
+        for (int j = tid; j < M; j += blockDim.x) { P[j] = 0.f; win[j] = 0; owner[j] = -1; }
+        if (tid == 0) { s_nact = 0; s_nmiss = 0; }  // (both return to 0 in every round's election)
         for (int i = tid; i < N; i += blockDim.x) rowcol[i] = -1;
         if (kc > 0)
             for (int i = tid; i < N; i += blockDim.x) ccnt[i] = 0;
@@ -293,8 +293,6 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
             __syncthreads();
             for (int it = 0; it < p.max_iter; ++it) {
                 // ---- active rows (their order does not change the round)
-                if (tid == 0) s_nact = 0;
-                __syncthreads();
                 for (int i = tid; i < N; i += blockDim.x)
                     if (rowcol[i] < 0) act[atomicAdd(&s_nact, 1)] = i;
                 __syncthreads();
@@ -304,8 +302,6 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
                     // ---- bids from the row caches (prices never fall, so a
                     //      cache whose second value is above its bound holds the
                     //      row's exact top-2); the misses go through the MMA
-                    if (tid == 0) s_nmiss = 0;
-                    __syncthreads();
                     for (int k = warp; k < K; k += ELA_IMP_THREADS / 32) {
                         const int i = act[k], n = ccnt[i];
                         Top2<float> tt;
@@ -404,13 +400,15 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
                 if (failed) break;
                 rounds++;
                 rowbids += K;
-                // ---- election: new price = max bid; the largest key within 1e-5 wins
-                for (int e = tid; e < K; e += blockDim.x) atomicMax(&maxb[lcol[e]], __float_as_uint(lbid[e]));
+                // ---- election: new price = max bid (in place: every bid is
+                //      above its column's price); the largest key within 1e-5
+                //      of it wins.  The round counters return to 0 here (all
+                //      threads read them before this round's first barrier).
+                for (int e = tid; e < K; e += blockDim.x) atomicMax(&Pbits[lcol[e]], __float_as_uint(lbid[e]));
                 __syncthreads();
                 for (int e = tid; e < K; e += blockDim.x) {
                     const int j = lcol[e];
-                    if (absval(sub_rn(lbid[e], __uint_as_float(maxb[j]))) < tol)
-                        atomicMax(&win[j], win_key(lrow[e], N, p.tie_rule));
+                    if (absval(sub_rn(lbid[e], P[j])) < tol) atomicMax(&win[j], win_key(lrow[e], N, p.tie_rule));
                 }
                 __syncthreads();
                 for (int e = tid; e < K; e += blockDim.x) {
@@ -422,11 +420,11 @@ __global__ void __launch_bounds__(ELA_IMP_THREADS, 1) implicit_kernel(const ImpP
                         rowcol[i] = j;
                     }
                 }
+                if (tid == 0) { s_nact = 0; s_nmiss = 0; }
                 __syncthreads();
-                for (int e = tid; e < K; e += blockDim.x) P[lcol[e]] = __uint_as_float(maxb[lcol[e]]);
-                __syncthreads();
-                for (int e = tid; e < K; e += blockDim.x) { maxb[lcol[e]] = 0u; win[lcol[e]] = 0; }
-                __syncthreads();
+                // win[] cleared before the next round's first barrier, which
+                // every thread passes only after its share of this loop
+                for (int e = tid; e < K; e += blockDim.x) win[lcol[e]] = 0;
             }
         }
         if (failed) break;
