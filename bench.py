@@ -459,12 +459,12 @@ def main():
         except Exception:
             peak_tf = 1590.0
         implicit = {"workload": "implicit C = Q K^T: B=256 N=M=512 D=16 bf16 (seed 3), eps 1e-2; no cost matrix, "
-                                "tcgen05 cost tiles every round",
+                                "tcgen05 cost tiles for the bidders whose row cache misses",
                     "problems_per_gpu": Bl, "ms_per_step": round(im, 4), "value": round(Bi / (im * 1e-3), 2),
                     "unit": "solves/sec", "scaling": "strong", "cost_bytes_read": 0,
                     "roofline": {"bound": "tensor", "achieved": round(tf, 4), "peak": peak_tf, "unit": "TFLOP/s",
                                  "frac": round(tf / peak_tf / world, 6),
-                                 "note": "round-latency bound: each round's MMA covers only its few bidders"}}
+                                 "note": "round-latency bound: algorithmic FLOPs (row-bids x M x D x 2) over the solve; cached bids skip the MMA, and a round's MMA covers only its few missing bidders"}}
 
     # the reference's own mode on the cfg2 matrix: constant epsilon 1e-2
     fixed = None
