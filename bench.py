@@ -13,7 +13,11 @@ ranks, not divided by N.  Also reported, each on its own line key:
                ranks (256/N problems each): solves/sec of the whole job;
   "cfg5":      config 5 (B=8, N=M=8192 bf16 integer costs, eps 1/8193,
                1000 rounds; the bandwidth-bound case) sharded 8/N per rank,
-               with its own HBM roofline.
+               with its own HBM roofline;
+  "round1":    the cfg2 matrix solved for one round (the whole launch);
+  "bid_pass":  the bid pass alone (ela_auction_compute_bids, the reference's
+               compute_bids) over every row of the cfg2 matrix and of the
+               local cfg5 shard, with its HBM roofline.
 The sharded legs gather their assignments after timing and check them: at
 N > 1 against a one-GPU solve of the whole batch on rank 0, at N = 1 (config
 4) against the CPU oracle.
@@ -256,6 +260,33 @@ def main():
         run.keep = (cst, ws, e)  # alive as long as run
         return run
 
+    def prepared_bids(cst, eps):
+        """One bid pass over every row of `cst` against zero prices through the
+        C ABI (ela_auction_compute_bids), outputs allocated once, here."""
+        import ctypes
+        lib = ela._lib.load()
+        B, N, M = cst.shape
+        pdt = torch.float64 if cst.dtype == torch.float64 else torch.float32
+        idx = torch.empty((B, N), dtype=torch.int64, device=dev)
+        inc = torch.empty((B, N), dtype=pdt, device=dev)
+        argv = (cst.data_ptr(), ela.solver.DTYPE_CODE[cst.dtype], B, N, M, cst.stride(0), cst.stride(1), None, None,
+                float(eps), idx.data_ptr(), inc.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+
+        def run():
+            ela._lib.check(lib.ela_auction_compute_bids(*argv), "ela_auction_compute_bids")
+            return idx, inc
+        run.keep = (cst,)
+        return run
+
+    def bid_pass_line(cst, eps, n, skip, flush_between, workload):
+        ms, _ = timed(prepared_bids(cst, eps), n, flush_between=flush_between)
+        ms = ms[skip:]
+        t = max_over_ranks(statistics.mean(ms))
+        nbytes = cst.numel() * cst.element_size()
+        ach = nbytes / (t * 1e-3) / 1e9
+        return {"workload": workload, "ms": round(t, 4), "alg_bytes": nbytes, "achieved": round(ach, 1),
+                "peak": measured_peak_hbm()[0], "unit": "GB/s", "frac": round(ach / measured_peak_hbm()[0], 4)}
+
     def timed(fn, n, flush_between=True):
         """Device ms of n calls of fn, every call bracketed by events on the
         stream and all enqueued before one synchronisation: the GPU runs ahead
@@ -326,6 +357,10 @@ def main():
               "achieved": round(r1_bytes / (r1_t * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
               "frac": round(r1_bytes / (r1_t * 1e-3) / 1e9 / peak, 4),
               "note": "whole launch (state init + bid pass + election), device time"}
+    # the bid pass alone (ela_auction_compute_bids, the reference's compute_bids):
+    # every row of the matrix against zero prices, one streaming pass from HBM
+    bid_pass = {"cfg2": bid_pass_line(cost, sched[0], args.warmup + args.steps, args.warmup, True,
+                                      "cfg2 matrix (64 MB), every row bids, L2 flushed between passes")}
 
     # e2e through the public API: pinned host cost -> device, solve, indices -> pinned host
     host_cost = cost_cpu.pin_memory()
@@ -512,6 +547,8 @@ def main():
                              "frac": round(ach5 / peak / world, 4), "alg_bytes_per_step": int(alg5),
                              "note": "frac per GPU: achieved / (peak x GPUs)"}}
         del solve5
+        bid_pass["cfg5"] = bid_pass_line(c5, eps5[0], 2 + max(3, min(args.steps, 10)), 2, False,
+                                         f"cfg5 batch ({hi - lo} x 8192^2 bf16, {c5.numel() * 2 >> 20} MB > L2), every row bids")
         cfg5["verified"] = gather_and_check(r5[0].clone(), B5, c5_all, eps5, 1000)
 
     cpu = None
@@ -545,6 +582,7 @@ def main():
             "cfg1": cfg1,
             "cfg3": cfg3,
             "round1": round1,
+            "bid_pass": bid_pass,
             "batched": batched,
             "implicit": implicit,
             "cfg5": cfg5,

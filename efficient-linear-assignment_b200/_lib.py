@@ -50,6 +50,9 @@ SIGNATURES = {
     "ela_auction_implicit_costs": (_c.c_int, [
         _c.c_void_p, _c.c_void_p, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_void_p,
         _c.c_void_p, _c.c_void_p]),
+    "ela_auction_compute_bids": (_c.c_int, [
+        _c.c_void_p, _c.c_int, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_int64, _c.c_void_p,
+        _c.c_void_p, _c.c_double, _c.c_void_p, _c.c_void_p, _c.c_void_p]),
     "ela_auction_set_wait_limit_ns": (None, [_c.c_uint64]),
     "ela_auction_debug_skip_arrive": (None, [_c.c_int]),
 }

@@ -2509,6 +2509,101 @@ auction_cluster_kernel(const Params p) {
 #undef ELA_CLUSTER_LEAVE
 }
 
+// ------------------------------------------------------- the bid pass alone
+// One round's bids of every unassigned row against given prices, as one
+// streaming pass over the cost rows: the reference's compute_bids
+// (src/csrc/interface.cpp:31-40 -> launch_bid_kernel_cuda,
+// src/csrc/kernels.cu:420-445) with the torch backend's column choice
+// (torch_backend.py:65-88).  HBM-bound: each row is read once, so the kernel
+// is a plain grid over every SM (two 256-thread CTAs per SM, each warp
+// scanning whole rows with ELA_BID_UNROLL 16-byte loads in flight per lane).
+// The problem's prices are staged in shared memory (zeros when none are
+// given).  Rows whose assignment is not -1 get column -1 and increment 0, as
+// in the reference.
+#define ELA_BID_THREADS 256
+#ifndef ELA_BID_UNROLL
+#define ELA_BID_UNROLL 8
+#endif
+
+struct BidParams {
+    const void* cost;
+    int64_t B, N, M, stride_b, stride_n;
+    const void* prices;         // B x M (R), or null: zeros
+    const int64_t* assign;      // B x N, or null: every row bids
+    double eps;
+    void* col_out;              // B x N, int64 (public entry) or int32 (the solve's first round)
+    void* inc_out;              // B x N increments (R): (v1 - v2) + eps
+    int vec_ok;
+    int col64;
+};
+
+template <typename In, typename R>
+__global__ void __launch_bounds__(ELA_BID_THREADS, 2) bid_pass_kernel(const BidParams q) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int M = (int)q.M;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    R* Ps = reinterpret_cast<R*>(smem);
+    const size_t poff = align_up(sizeof(R) * (size_t)M, 16);
+    R* scr_v = reinterpret_cast<R*>(smem + poff) + warp * ELA_SMALL_M;
+    int* scr_i = reinterpret_cast<int*>(smem + poff + sizeof(R) * (size_t)nw * ELA_SMALL_M) + warp * ELA_SMALL_M;
+    const PlainGeo g{M, q.vec_ok};
+    const R eps = (R)q.eps;
+    const R* pr = reinterpret_cast<const R*>(q.prices);
+    R* inc_out = reinterpret_cast<R*>(q.inc_out);
+    if (pr == nullptr)
+        for (int j = threadIdx.x; j < M; j += blockDim.x) Ps[j] = (R)0;
+    for (int64_t b = blockIdx.y; b < q.B; b += gridDim.y) {
+        if (pr != nullptr) {
+            __syncthreads();  // the previous problem's rows are done with Ps
+            for (int j = threadIdx.x; j < M; j += blockDim.x) Ps[j] = pr[b * q.M + j];
+        }
+        __syncthreads();
+        const In* base = reinterpret_cast<const In*>(q.cost) + b * q.stride_b;
+        for (int64_t i = (int64_t)blockIdx.x * nw + warp; i < q.N; i += (int64_t)gridDim.x * nw) {
+            const int64_t o = b * q.N + i;
+            int j1 = -1;
+            R inc = (R)0;
+            if (q.assign == nullptr || q.assign[o] == -1) {
+                const In* row = base + i * q.stride_n;
+                Top2<R> t;
+                if (!q.vec_ok) {
+                    t = scan_row_fast<In, R, NoSum, PlainGeo>(g, row, Ps, lane, 0, 1);
+                    if (t.v1 == t.v2) t = scan_row<In, R, NoSum, PlainGeo>(g, row, Ps, lane, 0, 1);
+                } else {
+                    const uint4* rv = reinterpret_cast<const uint4*>(row);
+                    const int nch = M / Elem<In>::W;
+                    top2_init(t);
+                    if (sizeof(In) == 2) {  // integer-like 16-bit costs tie often: one exact pass
+                        scan_chunks<In, R, ELA_BID_UNROLL, false>(rv, Ps, lane, 32, nch, t);
+                        t = top2_warp(t);
+                    } else {
+                        scan_chunks_fast<In, R, ELA_BID_UNROLL>(rv, Ps, lane, 32, nch, t);
+                        t = top2_warp_fast(t);
+                        if (t.v1 == t.v2) {  // tied maximum: the exact columns
+                            top2_init(t);
+                            scan_chunks<In, R, 4, false>(rv, Ps, lane, 32, nch, t);
+                            t = top2_warp(t);
+                        }
+                    }
+                }
+                R bid;
+                finish_bid<In, R, NoSum, PlainGeo>(g, row, Ps, t, eps, lane, scr_v, scr_i, j1, bid);
+                inc = add_rn(sub_rn(t.v1, t.v2), eps);
+            }
+            if (lane == 0) {
+                if (q.col64) reinterpret_cast<int64_t*>(q.col_out)[o] = j1;
+                else reinterpret_cast<int32_t*>(q.col_out)[o] = j1;
+                inc_out[o] = inc;
+            }
+        }
+    }
+}
+
+template <typename R>
+__host__ __device__ inline size_t bid_pass_smem(int64_t M) {
+    return align_up(sizeof(R) * (size_t)M, 16) + (sizeof(R) + sizeof(int)) * (size_t)(ELA_BID_THREADS / 32) * ELA_SMALL_M;
+}
+
 #include "ela_implicit.cuh"
 
 }  // namespace
@@ -2765,6 +2860,21 @@ int make_plan(int dtype, int64_t B, int64_t N, int64_t M, int path, Plan& pl, bo
         g_plans.emplace(key, pl);
     }
     return rc;
+}
+
+template <typename In, typename R>
+int launch_bid_pass(const BidParams& q, int ctas, cudaStream_t stream) {
+    const size_t bsm = bid_pass_smem<R>(q.M);
+    if (cudaFuncSetAttribute(bid_pass_kernel<In, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm) !=
+        cudaSuccess)
+        return ELA_ERR_CUDA;
+    const int64_t gy = q.B < 65535 ? q.B : 65535;
+    const int64_t rows_x = (q.N + ELA_BID_THREADS / 32 - 1) / (ELA_BID_THREADS / 32);
+    int64_t gx = (ctas + gy - 1) / gy;
+    if (gx > rows_x) gx = rows_x;
+    if (gx < 1) gx = 1;
+    bid_pass_kernel<In, R><<<dim3((unsigned int)gx, (unsigned int)gy), ELA_BID_THREADS, bsm, stream>>>(q);
+    return cudaGetLastError() == cudaSuccess ? ELA_OK : ELA_ERR_CUDA;
 }
 
 template <typename In, typename R>
@@ -3227,6 +3337,51 @@ int ela_auction_solve_noalloc(const void* cost, int dtype, int64_t B, int64_t N,
     if (status_out && cudaMemsetAsync(status_out, 0, 4, s) != cudaSuccess) return ELA_ERR_CUDA;
     if (stats_out && cudaMemsetAsync(stats_out, 0, (size_t)B * 32, s) != cudaSuccess) return ELA_ERR_CUDA;
     return dispatch(dtype, p, pl, s);
+}
+
+// The bid pass alone: the reference's compute_bids (src/csrc/interface.cpp:31-40).
+int ela_auction_compute_bids(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, int64_t stride_b,
+                             int64_t stride_n, const void* prices, const int64_t* assignment, double epsilon,
+                             int64_t* best_idx_out, void* increments_out, void* stream) {
+    const int es = elem_size(dtype);
+    if (es == 0 || B < 0 || N < 0 || M < 0) return ELA_ERR_ARGUMENT;
+    if (B == 0 || N == 0) return ELA_OK;
+    if (M < 2 || M >= (1ll << 30) || !cost || !best_idx_out || !increments_out) return ELA_ERR_ARGUMENT;
+    if (!(epsilon >= 0.0) || epsilon == INFINITY) return ELA_ERR_ARGUMENT;
+    if (stride_n < M || (B > 1 && stride_b < (N - 1) * stride_n + M)) return ELA_ERR_ARGUMENT;
+    int sms = 0;
+    size_t smem_max = 0, smem_sm = 0;
+    int rc = device_limits(sms, smem_max, smem_sm);
+    if (rc != ELA_OK) return rc;
+    const size_t bsm = (dtype == ELA_DTYPE_F64) ? bid_pass_smem<double>(M) : bid_pass_smem<float>(M);
+    if (bsm > smem_max) return ELA_ERR_UNSUPPORTED;  // the problem's prices are staged in shared memory
+    BidParams q = {};
+    q.cost = cost;
+    q.B = B; q.N = N; q.M = M; q.stride_b = stride_b; q.stride_n = stride_n;
+    q.prices = prices;
+    q.assign = assignment;
+    q.eps = epsilon;
+    q.col_out = best_idx_out;
+    q.inc_out = increments_out;
+    q.col64 = 1;
+    q.vec_ok = ((reinterpret_cast<uintptr_t>(cost) & 15u) == 0) && ((stride_n * es) % 16 == 0) &&
+               ((stride_b * es) % 16 == 0) && ((M * es) % 16 == 0);
+    const void* bk = (dtype == ELA_DTYPE_F64) ? (const void*)bid_pass_kernel<double, double>
+                   : (dtype == ELA_DTYPE_F16) ? (const void*)bid_pass_kernel<__half, float>
+                   : (dtype == ELA_DTYPE_BF16) ? (const void*)bid_pass_kernel<__nv_bfloat16, float>
+                                               : (const void*)bid_pass_kernel<float, float>;
+    int occ = 0;
+    if (cudaFuncSetAttribute(bk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bsm) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, bk, ELA_BID_THREADS, bsm) != cudaSuccess)
+        return ELA_ERR_CUDA;
+    if (occ < 1) return ELA_ERR_UNSUPPORTED;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    switch (dtype) {
+    case ELA_DTYPE_F32: return launch_bid_pass<float, float>(q, occ * sms, s);
+    case ELA_DTYPE_F16: return launch_bid_pass<__half, float>(q, occ * sms, s);
+    case ELA_DTYPE_BF16: return launch_bid_pass<__nv_bfloat16, float>(q, occ * sms, s);
+    default: return launch_bid_pass<double, double>(q, occ * sms, s);
+    }
 }
 
 #ifdef ELA_PROF

@@ -206,6 +206,43 @@ def solve_implicit(Q: torch.Tensor, K: torch.Tensor, epsilon: EpsArg = 1e-2, max
     return assign, prices, stats
 
 
+def compute_bids(cost: torch.Tensor, epsilon: float, prices: torch.Tensor | None = None,
+                 assignment: torch.Tensor | None = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """One round's bids: the reference's ``compute_bids`` (src/csrc/interface.cpp:31-40)
+    through the C ABI ``ela_auction_compute_bids``.  cost (B,N,M) or (N,M) CUDA
+    tensor (fp32/fp16/bf16/fp64, any row stride); prices (B,M) (fp32, fp64 for
+    fp64 costs; None = zeros); assignment (B,N) int64 (None = every row bids).
+    Returns (best_idx int64 (B,N), increments (B,N)): the column torch.topk
+    picks on -cost - prices and (v1 - v2) + epsilon for rows whose assignment
+    is -1; -1 and 0 for the others."""
+    squeeze = cost.dim() == 2
+    if squeeze:
+        cost = cost.unsqueeze(0)
+    if cost.dim() != 3 or not cost.is_cuda or cost.dtype not in DTYPE_CODE:
+        raise ValueError("compute_bids: cost must be a (B,N,M) CUDA tensor of fp32/fp16/bf16/fp64")
+    if cost.stride(2) != 1:
+        cost = cost.contiguous()
+    B, N, M = cost.shape
+    dev = cost.device
+    pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
+    if prices is not None:
+        prices = prices.reshape(B, M).to(device=dev, dtype=pdt).contiguous()
+    if assignment is not None:
+        assignment = assignment.reshape(B, N).to(device=dev, dtype=torch.int64).contiguous()
+    with torch.cuda.device(dev):
+        lib = _lib.load()
+        idx = torch.empty((B, N), dtype=torch.int64, device=dev)
+        inc = torch.empty((B, N), dtype=pdt, device=dev)
+        rc = lib.ela_auction_compute_bids(cost.data_ptr(), DTYPE_CODE[cost.dtype], B, N, M, cost.stride(0),
+                                          cost.stride(1), None if prices is None else prices.data_ptr(),
+                                          None if assignment is None else assignment.data_ptr(), float(epsilon),
+                                          idx.data_ptr(), inc.data_ptr(), torch.cuda.current_stream(dev).cuda_stream)
+        _lib.check(rc, "ela_auction_compute_bids")
+    if squeeze:
+        return idx[0], inc[0]
+    return idx, inc
+
+
 def implicit_costs(Q: torch.Tensor, K: torch.Tensor) -> torch.Tensor:
     """The (B,N,M) fp32 costs ``solve_implicit`` uses, written out by the same
     tensor-core instructions (C ABI ``ela_auction_implicit_costs``)."""

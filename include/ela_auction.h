@@ -175,6 +175,26 @@ int ela_auction_implicit_costs(const void* Q, const void* K, int dtype, int64_t 
                                float* cost_out, int32_t* status_out, void* stream);
 
 /*
+ * One round's bids, the reference's compute_bids(benefits, prices,
+ * assignment, best_idx, increments, epsilon) (src/csrc/interface.cpp:31-40,
+ * launch_bid_kernel_cuda in src/csrc/kernels.cu:420-445): for every row of
+ * every problem whose assignment is -1, the column it bids on and its
+ * increment (v1 - v2) + epsilon, where v = -cost - price over the row and
+ * (v1, v2) are its two largest values; the column is the one the torch
+ * backend's topk picks (torch_backend.py:65-88), ties included.  Rows already
+ * assigned get column -1 and increment 0.  cost as in ela_auction_solve;
+ * prices: device, contiguous B x M, float (double for fp64 costs), or NULL
+ * for all zeros; assignment: device int64 B x N, or NULL (every row bids);
+ * best_idx_out int64 B x N, increments_out float (double for fp64) B x N.
+ * One streaming pass over the rows (HBM-bound).  The problem's prices are
+ * staged in shared memory, so M is limited to what fits (ELA_ERR_UNSUPPORTED
+ * beyond).  Work is enqueued on `stream`; returns a status (ELA_OK ...).
+ */
+int ela_auction_compute_bids(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, int64_t stride_b,
+                             int64_t stride_n, const void* prices, const int64_t* assignment, double epsilon,
+                             int64_t* best_idx_out, void* increments_out, void* stream);
+
+/*
  * Limit, in nanoseconds, on every device-side wait of the grid path (each
  * round's exchange of bids between the CTAs that share one problem).  A wait that
  * runs out writes ELA_ERR_TIMEOUT to *status_out and the kernel returns.

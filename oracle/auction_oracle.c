@@ -306,3 +306,50 @@ int ela_oracle_solve(const void* cost, int dtype, int64_t B, int64_t N, int64_t 
     }
     return 0;
 }
+
+/*
+ * One round's bids (the checker of ela_auction_compute_bids): for every row
+ * whose assignment is -1 (or every row when assign is NULL), the column
+ * torch.topk(k=2) picks on v = (-c) - P and the increment (v1 - v2) + eps,
+ * exactly as one round of AuctionTorch.solve computes them
+ * (torch_backend.py:65-88); other rows get column -1 and increment 0, as the
+ * reference's compute_bids kernel writes (src/csrc/kernels.cu:53-57).
+ * prices: B*M float (double for fp64) or NULL (zeros).  inc_out: B*N float
+ * (double for fp64).  Returns 0, or 1 on a bad argument.
+ */
+#define DEFINE_BIDS(R, NAME, LOADER, TOPK)                                                       \
+    static void NAME(const void* cost, int dtype, int64_t off0, int64_t stride_n, int64_t N,    \
+                     int64_t M, const R* P, const int64_t* assign, double eps, int64_t* idx,    \
+                     R* inc) {                                                                   \
+        R* buf = (R*)malloc(sizeof(R) * (size_t)M);                                             \
+        for (int64_t i = 0; i < N; ++i) {                                                       \
+            if (assign && assign[i] != -1) { idx[i] = -1; inc[i] = (R)0; continue; }            \
+            LOADER(cost, dtype, off0 + i * stride_n, M, buf);                                   \
+            for (int64_t j = 0; j < M; ++j) buf[j] = buf[j] - (P ? P[j] : (R)0);                \
+            R v1, v2; int64_t j1;                                                               \
+            TOPK(buf, M, &v1, &v2, &j1);                                                        \
+            idx[i] = j1;                                                                        \
+            inc[i] = (v1 - v2) + (R)eps;                                                        \
+        }                                                                                       \
+        free(buf);                                                                              \
+    }
+
+DEFINE_BIDS(float, bids_one_f, load_row_f, topk_row_f)
+DEFINE_BIDS(double, bids_one_d, load_row_d, topk_row_d)
+
+int ela_oracle_bids(const void* cost, int dtype, int64_t B, int64_t N, int64_t M, int64_t stride_b,
+                    int64_t stride_n, const void* prices, const int64_t* assign, double eps,
+                    int64_t* idx_out, void* inc_out) {
+    if (B < 0 || N < 0 || M < 0 || dtype < 0 || dtype > 3) return 1;
+    if (N > 0 && M < 2) return 1;
+    for (int64_t b = 0; b < B; ++b) {
+        const int64_t* a = assign ? assign + b * N : NULL;
+        if (dtype == ELA_F64)
+            bids_one_d(cost, dtype, b * stride_b, stride_n, N, M, prices ? (const double*)prices + b * M : NULL, a,
+                       eps, idx_out + b * N, (double*)inc_out + b * N);
+        else
+            bids_one_f(cost, dtype, b * stride_b, stride_n, N, M, prices ? (const float*)prices + b * M : NULL, a,
+                       eps, idx_out + b * N, (float*)inc_out + b * N);
+    }
+    return 0;
+}

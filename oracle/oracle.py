@@ -88,6 +88,38 @@ def solve(cost: torch.Tensor, eps, max_iter: int = 1000, nthreads: int = 1, tie_
     return assign, prices, stats
 
 
+def bids(cost: torch.Tensor, eps: float, prices: torch.Tensor | None = None,
+         assignment: torch.Tensor | None = None):
+    """Oracle of one round's bids (the checker of ela_auction_compute_bids):
+    (B,N,M) CPU cost, optional (B,M) prices (float32, float64 for fp64 costs)
+    and (B,N) int64 assignment (-1 = bids).  Returns (best_idx int64 (B,N),
+    increments (B,N)): torch.topk's column on (-c) - P and (v1 - v2) + eps
+    (torch_backend.py:65-88); -1 and 0 for assigned rows."""
+    lib = _load()
+    if not hasattr(lib, "_bids_ready"):
+        lib.ela_oracle_bids.restype = ctypes.c_int
+        lib.ela_oracle_bids.argtypes = [
+            ctypes.c_void_p, ctypes.c_int, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+            ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_double, ctypes.c_void_p, ctypes.c_void_p]
+        lib._bids_ready = True
+    if cost.dim() == 2:
+        cost = cost.unsqueeze(0)
+    cost = cost.detach().cpu().contiguous()
+    B, N, M = cost.shape
+    pdt = torch.float64 if cost.dtype == torch.float64 else torch.float32
+    P = None if prices is None else prices.detach().cpu().to(pdt).contiguous()
+    A = None if assignment is None else assignment.detach().cpu().to(torch.int64).contiguous()
+    idx = torch.empty((B, N), dtype=torch.int64)
+    inc = torch.empty((B, N), dtype=pdt)
+    rc = lib.ela_oracle_bids(ctypes.c_void_p(cost.data_ptr()), DTYPE_CODE[cost.dtype], B, N, M, N * M, M,
+                             None if P is None else ctypes.c_void_p(P.data_ptr()),
+                             None if A is None else ctypes.c_void_p(A.data_ptr()), float(eps),
+                             ctypes.c_void_p(idx.data_ptr()), ctypes.c_void_p(inc.data_ptr()))
+    if rc != 0:
+        raise ValueError(f"oracle rejected arguments (status {rc})")
+    return idx, inc
+
+
 def solve_numpy(cost: np.ndarray, eps: float, max_iter: int = 1000):
     """Pure-numpy restatement of torch_backend.py:54-156 for one (N,M) problem.
 

@@ -65,3 +65,18 @@ def test_direct_solve_equals_padded_solve_when_dummy_rows_fit(shape, oracle_mod)
     ap, _, _ = oracle_mod.solve(padded, 1e-3, 2000)
     ad, _, _ = oracle_mod.solve(cost, 1e-3, 2000)
     assert torch.equal(ap[:, :N], ad)
+
+
+@pytest.mark.parametrize("M", [16, 96, 127, 128, 200])
+def test_oracle_bids_match_torch_topk(M, oracle_mod):
+    # one round's bids of the oracle against torch.topk itself (one thread, as
+    # the reference runs), on tie-heavy integer rows with a few price levels
+    torch.set_num_threads(1)
+    g = torch.Generator().manual_seed(M)
+    cost = torch.randint(0, 4, (2, 64, M), generator=g).float()
+    prices = torch.randint(0, 3, (2, M), generator=g).float() * 0.5
+    idx, inc = oracle_mod.bids(cost, 0.01, prices)
+    v = (-cost) - prices[:, None, :]
+    top = torch.topk(v, 2, dim=2)
+    assert torch.equal(idx, top.indices[..., 0])
+    assert torch.equal(inc, (top.values[..., 0] - top.values[..., 1]) + torch.tensor(0.01, dtype=torch.float32))
