@@ -59,12 +59,14 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffers) leg")
     ap.add_argument("--no-cfg5", action="store_true", help="skip the bandwidth-bound config-5 leg")
-    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4", "cfg4-shard8", "cfg2", "round1", "implicit"],
+    ap.add_argument("--profile-case", choices=["cfg5-small", "cfg4", "cfg4-shard8", "cfg2", "round1", "implicit",
+                                               "bidpass", "bidpass-cfg2"],
                     default=None,
                     help="run one small solve for an ncu capture and exit (cfg5-small: B=2 N=M=8192 "
                          "bf16, 256 MB > L2, max_iter 50; cfg4: the B=256 N=M=512 batch, 256 MB; cfg4-shard8: "
                          "its first 32 problems, one 8-GPU shard; cfg2: the headline solve, 64 MB; round1: the "
-                         "cfg2 matrix with max_iter 1, the full-matrix bid pass)")
+                         "cfg2 matrix with max_iter 1, the full-matrix bid pass; bidpass / bidpass-cfg2: "
+                         "ela_auction_compute_bids alone on 2 cfg5 problems (256 MB) / the cfg2 matrix)")
     ap.add_argument("--fixed-eps", action="store_true",
                     help="reference mode: constant epsilon 1e-2 instead of the cfg2 epsilon schedule")
     return ap.parse_args()
@@ -188,6 +190,15 @@ def profile_case(args):
             a, p, st = ela.solve_implicit(Q, K, 1e-2, 1000)
         torch.cuda.synchronize()
         print(json.dumps({"profile_case": "implicit", "row_bids": int(st[:, 1].sum().item())}))
+        return
+    if args.profile_case in ("bidpass", "bidpass-cfg2"):
+        # the bid pass alone: 2 problems of cfg5 (256 MB bf16 > L2) or the cfg2 matrix
+        c = ela.workloads.cfg2().cuda() if args.profile_case == "bidpass-cfg2" else \
+            ela.workloads.cfg5(8, 8192)[:2].contiguous().cuda()
+        for _ in range(2):
+            idx, inc = ela.compute_bids(c, 1.0)
+        torch.cuda.synchronize()
+        print(json.dumps({"profile_case": args.profile_case, "alg_bytes": c.numel() * c.element_size()}))
         return
     if args.profile_case == "cfg4":
         c, eps, mi, es = ela.workloads.cfg4().cuda(), [1e-2], 1000, 4
