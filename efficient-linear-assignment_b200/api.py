@@ -76,7 +76,7 @@ class AuctionIMLE(torch.autograd.Function):
         solver = _solver(ctx.backend_name, ctx.epsilon, ctx.max_iter)
         assignment_t = None
         if isinstance(solver, AuctionB200) and grad_output.shape == cost_matrix.shape \
-                and grad_output.dtype == cost_matrix.dtype:
+                and grad_output.dtype == cost_matrix.dtype and cost_matrix.is_cuda and grad_output.is_cuda:
             # the target cost C + lam*G is read from the two tensors by the
             # kernel (ela_auction_solve_sum), not built (reference api.py:106-111)
             from .solver import _as_schedule, auction_solve_sum
@@ -103,8 +103,11 @@ def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[
                       auto_pad: bool = False):
     """Solve the linear assignment problem (minimise total cost) by auction.
 
-    cost_matrix: (B,N,M) or (N,M) CUDA tensor, fp32/fp16/bf16/fp64, N and M
-    multiples of 8 (as in the reference) unless auto_pad.  epsilon: constant
+    cost_matrix: (B,N,M) or (N,M) tensor, fp32/fp16/bf16/fp64, N and M
+    multiples of 8 (as in the reference) unless auto_pad.  A CUDA tensor is
+    solved on its device; a host tensor (which the reference's backends also
+    take) is copied to the current CUDA device, solved there, and the result
+    comes back on the host.  There is no CPU solver: without a GPU this raises.  epsilon: constant
     epsilon (the reference's only mode) or an epsilon-scaling schedule.
     Returns (B,N) int64 indices when return_indices, else the differentiable
     (B,N,M) one-hot.
@@ -137,11 +140,17 @@ def linear_assignment(cost_matrix: torch.Tensor, epsilon: Union[float, Sequence[
             if return_indices:
                 if backend not in BACKENDS:
                     raise ValueError(f"Backend '{backend}' not available. Options: {list(BACKENDS.keys())}")
-                from .solver import _as_schedule, auction_solve_padded
+                from .solver import _as_schedule, _staging_device, auction_solve_padded
                 from . import _lib
-                assign, _, _, status = auction_solve_padded(cost_matrix.detach(), _as_schedule(epsilon), int(max_iter))
+                src = cost_matrix.detach()
+                on_host = not src.is_cuda
+                if on_host:  # host memory: solved on the current CUDA device, indices copied back
+                    src = src.to(_staging_device())
+                assign, _, _, status = auction_solve_padded(src, _as_schedule(epsilon), int(max_iter))
                 _lib.check(int(status.item()), "auction kernel")
                 idx = assign[:, :N].clamp(min=0)
+                if on_host:
+                    idx = idx.to(cost_matrix.device)
                 return idx if is_batched else idx.squeeze(0)
             from .utils import pad_input  # differentiable one-hot: autograd needs the padded tensor
             padded, _ = pad_input(cost_matrix)

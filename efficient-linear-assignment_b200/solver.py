@@ -345,6 +345,22 @@ class AuctionB200:
         self.last_stats = None
 
     def solve(self, cost_matrix: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """Solve on the GPU.  A cost in host memory (the reference's backends
+        accept CPU tensors) is copied to the current CUDA device, solved there
+        by the same kernels, and the results are copied back to its device;
+        without a CUDA device this raises (there is no CPU solver)."""
+        if not cost_matrix.is_cuda:
+            dev = _staging_device()
+            assign, prices = self.solve(cost_matrix.to(dev))
+            return assign.to(cost_matrix.device), prices.to(cost_matrix.device)
         assign, prices, stats = solve(cost_matrix, self.epsilon, self.max_iter, self.path, tie_rule=self.tie_rule)
         self.last_stats = stats
         return assign, prices
+
+
+def _staging_device() -> torch.device:
+    """The CUDA device a host-memory cost is solved on (the current one)."""
+    if not torch.cuda.is_available():
+        raise RuntimeError("the B200 auction solver needs a CUDA device; none is visible "
+                           "(there is no CPU fallback)")
+    return torch.device("cuda", torch.cuda.current_device())

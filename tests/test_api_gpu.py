@@ -185,3 +185,34 @@ def test_eager_entry_equals_custom_op(shape, path):
         assert int(got[3].item()) == 0
         for g, r in zip(got, ref):
             assert torch.equal(g, r)
+
+
+def test_host_tensor_is_solved_on_the_gpu(oracle_mod):
+    # the reference's linear_assignment takes CPU tensors; here a host cost is
+    # copied to the current GPU, solved by the same kernels, and the indices
+    # come back on the host, equal to the oracle's
+    cost = ela.workloads.cfg1()
+    idx = ela.linear_assignment(cost, epsilon=1e-2)
+    assert idx.device.type == "cpu"
+    a, _, _ = oracle_mod.solve(cost, 1e-2, 1000)
+    assert torch.equal(idx, a.clamp(min=0))
+    a2, p2 = ela.AuctionB200(1e-2, 1000).solve(cost)
+    assert a2.device.type == "cpu" and p2.device.type == "cpu" and torch.equal(a2, a)
+    # auto_pad through the host path
+    odd = torch.rand(2, 20, 21, generator=torch.Generator().manual_seed(3))
+    assert torch.equal(ela.linear_assignment(odd, auto_pad=True),
+                       ela.linear_assignment(odd.cuda(), auto_pad=True).cpu())
+
+
+def test_host_tensor_one_hot_and_backward_match_device():
+    g = torch.Generator().manual_seed(12)
+    base = torch.rand(2, 64, 64, generator=g)
+    grad = torch.randn(2, 64, 64, generator=g)
+    c_host = base.clone().requires_grad_(True)
+    P_host = ela.linear_assignment(c_host, epsilon=1e-2, return_indices=False)
+    (P_host * grad).sum().backward()
+    c_dev = base.cuda().requires_grad_(True)
+    P_dev = ela.linear_assignment(c_dev, epsilon=1e-2, return_indices=False)
+    (P_dev * grad.cuda()).sum().backward()
+    assert P_host.device.type == "cpu" and torch.equal(P_host, P_dev.cpu())
+    assert torch.equal(c_host.grad, c_dev.grad.cpu())
