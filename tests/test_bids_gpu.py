@@ -88,3 +88,11 @@ def test_bids_rejects_bad_arguments():
         ela.compute_bids(torch.rand(2, 8, 1).cuda(), 0.1)   # M < 2: no second value
     with pytest.raises(_lib.AuctionError):
         ela.compute_bids(torch.rand(2, 8, 16).cuda(), float("inf"))
+
+
+def test_bids_report_unsupported_when_prices_do_not_fit():
+    # the problem's prices are staged in shared memory: a row longer than that
+    # holds is refused with ELA_ERR_UNSUPPORTED, not run
+    with pytest.raises(_lib.AuctionError) as e:
+        ela.compute_bids(torch.rand(1, 8, 64000).cuda(), 0.1)
+    assert e.value.status == _lib.ELA_ERR_UNSUPPORTED
